@@ -1,0 +1,406 @@
+"""Benchmark: attention fwd+bwd TFLOP/s on B200 (1..8 GPUs), one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workload (default "c4"): causal fwd+bwd, B=8, S=8192, H=32, D=128, fp16,
+q/k/v/dO ~ N(0,1) from seeded generators (synthetic data).  The 256
+(batch, head) pairs are split by batch across the N ranks with no collective
+(strong scaling: the total work is fixed).  One step = out = flash_attn(q, k, v,
+causal=True); out.backward(dO) through the public autograd API.
+FLOPs (benchmark convention): 4*B*H*S^2*D, halved for causal; fwd+bwd = 2.5x.
+
+Extra keys beside the base contract:
+  e2e          the same step with pinned-host inputs copied in and O, dQ, dK,
+               dV copied back inside the timed region.
+  roofline     the dominant kernel (the main backward kernel) timed alone with
+               CUDA events; achieved = its algorithmic tensor FLOPs (5 GEMMs,
+               2.5 x F_fwd) / its mean duration; peak = MEASURED_PEAKS.json.
+  cpu_baseline the CPU oracle (restatement of the reference's fp32 eager path)
+               on one (batch, head) pair of the same workload, rank 0, N=1.
+  headline_c3b the headline config (B=1, S=4096, H=8, D=128, causal) at N=1.
+  clocks       nvidia-smi samples taken during the timed region.
+--impl reference times the reference's CPU path (the oracle port) on the host
+cores, each step = fwd+bwd of one (batch, head) pair of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+WORKLOADS = {
+    # name: (B, S, H, D, causal, amp)
+    "c4": (8, 8192, 32, 128, True, 1.0),
+    "c3b": (1, 4096, 8, 128, True, 0.5),
+    "c3a": (1, 4096, 16, 64, True, 0.5),
+    "c1": (2, 1024, 8, 64, False, 1.0),
+}
+
+
+def flops_fwd(B, S, H, D, causal):
+    f = 4.0 * B * H * S * S * D
+    return f * 0.5 if causal else f
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops"), d.get("bf16_tflops_sustained"), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def gen_shard(B0, B1, S, H, D, amp, device, seed_base=1234):
+    """q, k, v, dO for batches [B0, B1) — each batch index has its own seed so
+    every GPU count sees the same global tensors."""
+    outs = [torch.empty((B1 - B0, S, H, D), dtype=torch.float16, device=device) for _ in range(4)]
+    for i, b in enumerate(range(B0, B1)):
+        g = torch.Generator(device=device).manual_seed(seed_base + b)
+        for t in outs:
+            t[i].normal_(0.0, 1.0, generator=g)
+            if amp != 1.0:
+                t[i].mul_(amp)
+    return outs
+
+
+# ----------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------- CPU path
+def cpu_pair_step(S, D, causal, amp, seed=0):
+    """One fwd+bwd of one (batch, head) pair through the CPU oracle (fp32)."""
+    from oracle.attention_oracle import attention_fwd
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, do = [(torch.randn((1, S, 1, D), generator=g) * amp).half() for _ in range(4)]
+    leaves = [t.float().requires_grad_() for t in (q, k, v)]
+    t0 = time.perf_counter()
+    o, _ = attention_fwd(*leaves, causal=causal, dtype=torch.float32)
+    o.backward(do.float())
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(S, D, causal, amp, budget_s=20.0):
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_pair_step(min(S, 1024), D, causal, amp)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while not times or (time.perf_counter() - t_start < budget_s and len(times) < 5):
+        times.append(cpu_pair_step(S, D, causal, amp, seed=len(times)))
+    t = statistics.median(times)
+    f = 2.5 * flops_fwd(1, S, 1, D, causal)
+    return {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{len(times)} x fwd+bwd of one (batch, head) pair, S={S}, D={D}, "
+                      f"causal={causal}, fp32 oracle (ref.py eager restated), median "
+                      f"{t:.3f} s per pair"}
+
+
+def run_reference(args, wl):
+    world, rank, _ = dist_env()
+    B, S, H, D, causal, amp = WORKLOADS[wl]
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    for i in range(args.warmup):
+        cpu_pair_step(S, D, causal, amp, seed=100 + i)
+    times = [cpu_pair_step(S, D, causal, amp, seed=i) for i in range(args.steps)]
+    t = sum(times)
+    f = 2.5 * flops_fwd(1, S, 1, D, causal) * len(times)
+    val = f / t / 1e12
+    line = {
+        "impl": "reference", "metric": "attention fwd+bwd TFLOP/s", "value": val,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / len(times), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl, "B": B, "S": S, "H": H, "D": D, "causal": causal,
+                   "step": "fwd+bwd of one (batch, head) pair on the host CPU",
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{len(times)} steps x one (b,h) pair, S={S}, D={D}"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------- GPU path
+def time_steps(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_ours(args, wl):
+    import torch.distributed as dist
+    from flash_attn_volta_b200 import _lib, check_status, flash_attn, flash_attn_forward
+    from flash_attn_volta_b200.forward import _stream_ptr
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, S, H, D, causal, amp = WORKLOADS[wl]
+    assert B % world == 0, f"batch {B} not divisible by {world} GPUs"
+    b0, b1 = rank * B // world, (rank + 1) * B // world
+    q, k, v, do = gen_shard(b0, b1, S, H, D, amp, dev)
+    q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        out = flash_attn(q, k, v, causal=causal)
+        out.backward(do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    check_status(dev)
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
+    ms = time_steps(step, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    clock_info = clocks.stop() if clocks else None
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    check_status(dev)
+    total_flops = 2.5 * flops_fwd(B, S, H, D, causal) * args.steps
+    value = total_flops / (ms * 1e-3) / 1e12
+
+    # ---------------- e2e: pinned host -> device, step, results -> pinned host
+    hq, hk, hv, hdo = [t.detach().cpu().pin_memory() for t in (q, k, v, do)]
+    hout = [torch.empty_like(hq).pin_memory() for _ in range(4)]
+    dq_, dk_, dv_ = (torch.empty_like(q) for _ in range(3))
+
+    def e2e_step():
+        qd = torch.empty_like(q).copy_(hq, non_blocking=True).requires_grad_()
+        kd = torch.empty_like(k).copy_(hk, non_blocking=True).requires_grad_()
+        vd = torch.empty_like(v).copy_(hv, non_blocking=True).requires_grad_()
+        dod = torch.empty_like(do).copy_(hdo, non_blocking=True)
+        out = flash_attn(qd, kd, vd, causal=causal)
+        out.backward(dod)
+        for h_, d_ in zip(hout, (out, qd.grad, kd.grad, vd.grad)):
+            h_.copy_(d_.detach(), non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e2e_ms = time_steps(e2e_step, e2e_steps, stream)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = 2.5 * flops_fwd(B, S, H, D, causal) * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    nb = q.numel() * 2
+    del hout
+
+    # ---------------- dominant kernel alone: main backward kernel
+    lib = _lib.load()
+    with torch.no_grad():
+        qq, kk_, vv = q.detach(), k.detach(), v.detach()
+        o, lse = flash_attn_forward(qq, kk_, vv, causal=causal, return_softmax_lse=True)
+        Bl = qq.shape[0]
+        nbytes = lib.fa_sm100_bwd_workspace_bytes(Bl, S, H, D)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        status = _lib.status_word(dev)
+        scale = 1.0 / math.sqrt(D)
+
+        def phase(p):
+            rc = lib.fa_sm100_bwd_phase(p, do.data_ptr(), qq.data_ptr(), kk_.data_ptr(),
+                                        vv.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                        dq_.data_ptr(), dk_.data_ptr(), dv_.data_ptr(),
+                                        ws.data_ptr(), nbytes, Bl, S, H, D, scale,
+                                        1 if causal else 0, status.data_ptr(), _stream_ptr(dev))
+            _lib.check(rc, "fa_sm100_bwd_phase")
+
+        phase(0)
+        reps = max(3, min(args.steps, 10))
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(reps)]
+        phase(1)
+        for e0, e1 in ev:
+            e0.record(stream)
+            phase(1)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        k_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+        # forward kernel alone, same method
+        evf = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for e0, e1 in evf:
+            e0.record(stream)
+            flash_attn_forward(qq, kk_, vv, causal=causal)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        f_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evf)
+        check_status(dev)
+        del ws
+    peak_burst, peak_sus, peak_kind = load_peaks()
+    bwd_alg = 2.5 * flops_fwd(Bl, S, H, D, causal)      # 5 GEMMs of the backward
+    fwd_alg = flops_fwd(Bl, S, H, D, causal)            # 2 GEMMs of the forward
+    k_tflops = bwd_alg / (k_ms * 1e-3) / 1e12
+    f_tflops = fwd_alg / (f_ms * 1e-3) / 1e12
+
+    headline = None
+    if rank == 0 and world == 1 and wl != "c3b":
+        headline = bench_small("c3b", dev, args)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(S, D, causal, amp, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": "attention fwd+bwd TFLOP/s",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": wl, "B": B, "S": S, "H": H, "D": D, "causal": causal,
+                       "global_batch": B, "seq_len": S, "parallelism": f"batch-shard{world}",
+                       "flops_per_step": 2.5 * flops_fwd(B, S, H, D, causal),
+                       "flop_convention": "4*B*H*S^2*D (/2 causal), fwd+bwd = 2.5x",
+                       "l2": "inputs (512 MiB per tensor at N=1) larger than the 126 MB L2"},
+            "pct_of_peak": {"value": value / (peak_sus if peak_sus else peak_burst),
+                            "peak_tflops": peak_sus, "kind": f"{peak_kind} bf16 sustained"},
+            "gpu_launches": 4 * args.steps,
+            "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nb,
+                    "d2h_bytes_per_step": 4 * nb, "steps": e2e_steps},
+            "roofline": {"bound": "tensor", "kernel": f"fa_bwd_main_kernel<{D}>",
+                         "achieved": k_tflops, "peak": peak_burst, "unit": "TFLOP/s",
+                         "frac": k_tflops / peak_burst, "traffic": None,
+                         "peak_kind": f"{peak_kind} bf16 burst",
+                         "flops_per_launch": bwd_alg, "mean_ms": k_ms,
+                         "fwd_kernel": {"achieved": f_tflops, "mean_ms": f_ms,
+                                        "frac": f_tflops / peak_burst}},
+            "clocks": clock_info,
+        }
+        if headline:
+            line["headline_c3b"] = headline
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_small(wl, dev, args):
+    """fwd+bwd of a small workload, L2 flushed between steps."""
+    from flash_attn_volta_b200 import flash_attn
+    B, S, H, D, causal, amp = WORKLOADS[wl]
+    q, k, v, do = gen_shard(0, B, S, H, D, amp, dev)
+    q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ts = []
+    for i in range(5 + 20):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        q.grad = k.grad = v.grad = None
+        out = flash_attn(q, k, v, causal=causal)
+        out.backward(do)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= 5:
+            ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    f = 2.5 * flops_fwd(B, S, H, D, causal)
+    return {"B": B, "S": S, "H": H, "D": D, "causal": causal, "ms_per_step": ms,
+            "tflops": f / (ms * 1e-3) / 1e12, "l2": "flushed (256 MiB write) before each step"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args, args.workload)
+    else:
+        run_ours(args, args.workload)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,98 @@
+"""ctypes binding of libfa_sm100.so (the C ABI in include/fa_sm100.h).
+
+The library is loaded once, from this package's directory.  There is no
+fallback: if the library is missing, every entry point raises RuntimeError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from .build import lib_path
+
+FA_OK = 0
+FA_ERR_ARG = 1
+FA_ERR_TMA = 2
+FA_ERR_LAUNCH = 3
+FA_ERR_DEVICE = 4
+FA_ERR_WORKSPACE = 5
+
+STATUS_TIMEOUT = 1
+
+_lock = threading.Lock()
+_lib = None
+
+_c_int, _c_float, _vp, _c_size = ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
+
+
+def load() -> ctypes.CDLL:
+    """Load libfa_sm100.so (raises RuntimeError when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            if not os.path.exists(path):
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python -m flash_attn_volta_b200.build` "
+                    "(the CUDA kernels have no fallback)")
+            lib = ctypes.CDLL(path)
+            lib.fa_sm100_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                         _c_float, _c_int, _vp, _vp]
+            lib.fa_sm100_fwd.restype = _c_int
+            lib.fa_sm100_bwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_size,
+                                         _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp,
+                                         _vp]
+            lib.fa_sm100_bwd.restype = _c_int
+            lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes
+            lib.fa_sm100_bwd_phase.restype = _c_int
+            lib.fa_sm100_bwd_workspace_bytes.argtypes = [_c_int, _c_int, _c_int, _c_int]
+            lib.fa_sm100_bwd_workspace_bytes.restype = _c_size
+            lib.fa_sm100_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
+            lib.fa_sm100_set_wait_timeout_ns.restype = None
+            lib.fa_sm100_error_string.argtypes = [_c_int]
+            lib.fa_sm100_error_string.restype = ctypes.c_char_p
+            lib.fa_sm100_abi_version.argtypes = []
+            lib.fa_sm100_abi_version.restype = _c_int
+            _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FA_OK:
+        msg = load().fa_sm100_error_string(rc).decode()
+        raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+
+
+# ----------------------------------------------------------------- status word
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels OR error bits into (1 = on-device wait timed out)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Synchronise and raise RuntimeError if a kernel on `device` reported an error."""
+    devs = [device] if device is not None else [torch.device("cuda", i) for i in _status]
+    for d in devs:
+        t = status_word(d)
+        v = int(t.item())
+        if v:
+            t.zero_()
+            raise RuntimeError(f"flash_attn_volta_b200 kernel reported status {v} on {d} "
+                               "(1 = an on-device wait timed out)")
+
+
+def debug_sync() -> bool:
+    return os.environ.get("FA_B200_SYNC_CHECK", "0") == "1"

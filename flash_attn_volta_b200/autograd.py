@@ -1,0 +1,52 @@
+"""Autograd-aware entry point (drop-in for flash_attn_volta/autograd.py:19-59).
+
+`_FlashAttnFn.forward` runs the forward with LSE and saves (q, k, v, out, lse)
+plus causal / sm_scale; `backward` makes dO contiguous, casts it to q's dtype
+(autograd.py:37-39) and runs the backward.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .backward import flash_attn_backward
+from .forward import flash_attn_forward
+
+
+class _FlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal: bool, sm_scale: float | None):
+        if sm_scale is None:
+            sm_scale = 1.0 / math.sqrt(q.shape[-1])
+        out, lse = flash_attn_forward(q, k, v, causal=causal, sm_scale=sm_scale,
+                                      return_softmax_lse=True)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal = causal
+        ctx.sm_scale = sm_scale
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, out, lse = ctx.saved_tensors
+        do = do.contiguous()
+        if do.dtype != q.dtype:
+            do = do.to(q.dtype)
+        dq, dk, dv = flash_attn_backward(do, q, k, v, out, lse,
+                                         causal=ctx.causal, sm_scale=ctx.sm_scale)
+        return dq, dk, dv, None, None
+
+
+def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               causal: bool = False, sm_scale: float | None = None) -> torch.Tensor:
+    """Autograd-aware FlashAttention on B200.
+
+    Args:
+        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.
+        causal:  lower-triangular (top-left) mask if True.
+        sm_scale: softmax scale (default 1/sqrt(D)).
+
+    Returns:
+        out: (B, N, H, D) fp16, with autograd hooked up.
+    """
+    return _FlashAttnFn.apply(q, k, v, causal, sm_scale)

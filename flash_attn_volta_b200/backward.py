@@ -1,0 +1,71 @@
+"""Attention backward entry point (drop-in for flash_attn_volta/triton_fa_bwd.py:587-700).
+
+`flash_attn_backward(do, q, k, v, o, lse, causal, sm_scale) -> (dq, dk, dv)`
+keeps the reference's signature, AssertionError checks (triton_fa_bwd.py:609-614,
+:646) and default scale.  delta = rowsum(O*dO), the five backward GEMMs and
+the dQ conversion all run on the GPU behind fa_sm100_bwd; the fp32 workspace
+it needs comes from the torch caching allocator and is released on return.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from .forward import _as_kernel_input, _stream_ptr
+
+
+def flash_attn_backward(
+    do: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    lse: torch.Tensor,
+    causal: bool = False,
+    sm_scale: float | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """FlashAttention backward on B200 — fp16 in/out, fp32 accumulation.
+
+    Args:
+        do: (B, N, H, D) fp16, gradient w.r.t. output.
+        q, k, v, o: (B, N, H, D) fp16 forward inputs and output.
+        lse: (B, H, N) fp32 log-sum-exp from the forward (+inf on fully masked rows).
+        causal, sm_scale: must match the forward call.
+
+    Returns:
+        (dq, dk, dv), each (B, N, H, D) fp16.
+    """
+    assert q.is_cuda and k.is_cuda and v.is_cuda and o.is_cuda and do.is_cuda
+    assert q.dtype == torch.float16 == k.dtype == v.dtype == o.dtype == do.dtype
+    assert lse.dtype == torch.float32
+    assert q.shape == k.shape == v.shape == o.shape == do.shape
+    B, N, H, D = q.shape
+    assert D in (16, 32, 64, 128), f"unsupported head_dim {D}"
+    assert lse.shape == (B, H, N), f"lse shape {lse.shape} expected ({B},{H},{N})"
+
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+
+    do, q, k, v, o = (_as_kernel_input(t) for t in (do, q, k, v, o))
+    lse = lse.contiguous()
+    dq = torch.empty((B, N, H, D), dtype=torch.float16, device=q.device)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    if q.numel() == 0:
+        return dq, dk, dv
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        nbytes = lib.fa_sm100_bwd_workspace_bytes(B, N, H, D)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        status = _lib.status_word(q.device)
+        rc = lib.fa_sm100_bwd(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                              o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                              dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, D,
+                              float(sm_scale), 1 if causal else 0, status.data_ptr(),
+                              _stream_ptr(q.device))
+    _lib.check(rc, "fa_sm100_bwd")
+    if _lib.debug_sync():
+        _lib.check_status(q.device)
+    return dq, dk, dv

@@ -1,0 +1,215 @@
+// C ABI of libfa_sm100.so (declared in include/fa_sm100.h): argument checks,
+// TMA tensor-map construction over the caller's (B, S, H, D) buffers, workspace
+// carving and kernel launches.  Holds no per-call state.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "fa_kernels.h"
+
+namespace fa_sm100 {
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::atomic<unsigned long long> g_timeout_ns{4000000000ull};
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// The current device must be compute capability 10.0 (B200 / sm_100a).
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_DEVICE;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return FA_ERR_DEVICE;
+  return (major == 10 && minor == 0) ? FA_OK : FA_ERR_DEVICE;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool valid_shape(int B, int S, int H, int D) {
+  return B > 0 && S > 0 && H > 0 && (D == 16 || D == 32 || D == 64 || D == 128) &&
+         (long long)B * H < 65536LL * 65535LL;
+}
+
+// Tensor map over a contiguous (B, S, H, D) fp16 tensor; a box is `rows`
+// consecutive sequence positions of one (b, h) and one swizzle-width slice of D.
+int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, int rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return FA_ERR_DEVICE;
+  const int swb = D * 2 >= 128 ? 128 : D * 2;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)H * D * 2, (cuuint64_t)D * 2,
+                                 (cuuint64_t)S * H * D * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)(swb / 2), (cuuint32_t)rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle swz = swb == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TMA;
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t dq_acc, lse2, delta, total;
+};
+
+WsLayout ws_layout(int B, int S, int H, int D) {
+  const size_t S_pad = round_up((size_t)S, kSeqPad);
+  const size_t rows = (size_t)B * H * S_pad;
+  WsLayout w;
+  w.dq_acc = 0;
+  w.lse2 = round_up(rows * D * sizeof(float), 256);
+  w.delta = w.lse2 + round_up(rows * sizeof(float), 256);
+  w.total = w.delta + round_up(rows * sizeof(float), 256);
+  return w;
+}
+
+}  // namespace
+}  // namespace fa_sm100
+
+using namespace fa_sm100;
+
+extern "C" {
+
+int fa_sm100_abi_version(void) { return FA_SM100_ABI_VERSION; }
+
+const char* fa_sm100_error_string(int code) {
+  switch (code) {
+    case FA_OK: return "ok";
+    case FA_ERR_ARG: return "invalid argument (shape, head_dim, null or misaligned pointer)";
+    case FA_ERR_TMA: return "TMA tensor map encoding failed";
+    case FA_ERR_LAUNCH: return "kernel launch failed";
+    case FA_ERR_DEVICE: return "current device is not sm_100 or the driver entry point is missing";
+    case FA_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown error";
+  }
+}
+
+void fa_sm100_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 1ull); }
+
+int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
+                 int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
+                 void* stream) {
+  if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  if (!q || !k || !v || !out || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return FA_ERR_ARG;
+  if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return FA_ERR_ARG;
+  int rc = check_device();
+  if (rc != FA_OK) return rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  FwdArgs a;
+  a.tm_q = &tq;
+  a.tm_k = &tk;
+  a.tm_v = &tv;
+  a.o = out;
+  a.lse = lse;
+  a.B = batch;
+  a.S = seqlen;
+  a.H = nheads;
+  a.D = head_dim;
+  a.scale = sm_scale;
+  a.causal = causal ? 1 : 0;
+  a.status = status;
+  a.timeout_ns = g_timeout_ns.load();
+  return launch_fwd(a, static_cast<cudaStream_t>(stream));
+}
+
+size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim) {
+  if (!valid_shape(batch, seqlen, nheads, head_dim)) return 0;
+  return ws_layout(batch, seqlen, nheads, head_dim).total;
+}
+
+static int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
+                    const void* out, const float* lse, void* dq, void* dk, void* dv,
+                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
+                    int head_dim, float sm_scale, int causal, int* status, void* stream) {
+  if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  const void* ptrs[] = {dout, q, k, v, out, dq, dk, dv};
+  for (const void* p : ptrs)
+    if (!p || !aligned16(p)) return FA_ERR_ARG;
+  if (!lse || (reinterpret_cast<uintptr_t>(lse) & 3u)) return FA_ERR_ARG;
+  const WsLayout w = ws_layout(batch, seqlen, nheads, head_dim);
+  if (!workspace || workspace_bytes < w.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return FA_ERR_WORKSPACE;
+  int rc = check_device();
+  if (rc != FA_OK) return rc;
+  const int qrows = bwd_q_rows(head_dim);
+  CUtensorMap tq, tdo, tk, tv;
+  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tdo, dout, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  BwdArgs a;
+  a.tm_q = &tq;
+  a.tm_do = &tdo;
+  a.tm_k = &tk;
+  a.tm_v = &tv;
+  a.o = out;
+  a.dout = dout;
+  a.lse = lse;
+  a.dq = dq;
+  a.dk = dk;
+  a.dv = dv;
+  a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
+  a.lse2 = reinterpret_cast<float*>(ws + w.lse2);
+  a.delta = reinterpret_cast<float*>(ws + w.delta);
+  a.B = batch;
+  a.S = seqlen;
+  a.H = nheads;
+  a.D = head_dim;
+  a.S_pad = (int)round_up((size_t)seqlen, kSeqPad);
+  a.scale = sm_scale;
+  a.causal = causal ? 1 : 0;
+  a.status = status;
+  a.timeout_ns = g_timeout_ns.load();
+  return launch_bwd(a, static_cast<cudaStream_t>(stream), phase);
+}
+
+int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, const void* out,
+                 const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                 size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
+                 float sm_scale, int causal, int* status, void* stream) {
+  return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
+                  seqlen, nheads, head_dim, sm_scale, causal, status, stream);
+}
+
+int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
+                       const void* out, const float* lse, void* dq, void* dk, void* dv,
+                       void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
+                       int head_dim, float sm_scale, int causal, int* status, void* stream) {
+  if (phase < 0 || phase > 2) return FA_ERR_ARG;
+  return bwd_impl(phase, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
+                  seqlen, nheads, head_dim, sm_scale, causal, status, stream);
+}
+
+}  // extern "C"

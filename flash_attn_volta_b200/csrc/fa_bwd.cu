@@ -1,0 +1,484 @@
+// FlashAttention backward for sm_100a (B200).
+//
+// Replaces the reference's backward (flash_attn_volta/triton_fa_bwd.py):
+//   delta = rowsum(O * dO)                              (:650, torch op there)
+//   P  = exp(S - LSE),  S = scale * Q K^T               (:123-165, :355-411)
+//   dV = P^T dO,  dP = dO V^T,  dS = P (dP - delta)      (:169-172, :415-422)
+//   dK = scale * dS^T Q,  dQ = scale * dS K             (:176-178, :426-429)
+// The reference runs two kernels (dQ parallel over query blocks, dK/dV parallel
+// over key blocks) with 7 GEMMs; here one kernel per key block computes all
+// five GEMMs and accumulates dQ into an fp32 workspace with L2 reductions.
+//
+// Kernels:
+//   fa_bwd_pre   delta (fp32), LSE * log2(e), zero the dQ accumulator.
+//   fa_bwd_main  one CTA = one 128-row key/value tile of one (batch, head);
+//                loops over query tiles of BM rows (64 for D=128, else 128).
+//     warps 0-3  "softmax": thread r owns key row r.  Reads S^T and dP^T from
+//                tensor memory, P^T = exp2(S^T*scale*log2e - LSE2),
+//                dS^T = P^T (dP^T - delta), writes both (fp16) to shared memory;
+//                final dK/dV epilogue.
+//     warps 4-7  dQ epilogue: read this tile's dQ partial from tensor memory and
+//                add it into the fp32 accumulator (global reductions).
+//     warp 8     TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
+//     warp 9     MMA issuer: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO,
+//                dK += dS^T Q, dQ partial = dS K (stored transposed for D=128).
+//   fa_bwd_post  dQ = fp16(scale * accumulator) in (B, S, H, D).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "fa_kernels.h"
+#include "sm100_ptx.cuh"
+
+namespace fa_sm100 {
+
+template <int D>
+struct BwdCfg {
+  static constexpr int BN = 128;                    // key rows per CTA
+  static constexpr int BM = (D == 128) ? 64 : 128;  // query rows per iteration
+  static constexpr bool DQT = (D == 128);           // dQ accumulated transposed (M = D)
+  static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;
+  static constexpr int AE = SWB / 2;
+  static constexpr int NAT = D / AE;
+  static constexpr int NST = 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int PT_BYTES = BN * BM * 2;  // [key row][query col], 64-col atoms
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_BYTES;
+  static constexpr int OFF_Q = OFF_V + KV_BYTES;
+  static constexpr int OFF_DO = OFF_Q + NST * Q_BYTES;
+  static constexpr int OFF_LSE = OFF_DO + NST * Q_BYTES;
+  static constexpr int OFF_DELTA = OFF_LSE + NST * BM * 4;
+  static constexpr int OFF_P = ((OFF_DELTA + NST * BM * 4) + 1023) / 1024 * 1024;
+  static constexpr int OFF_DS = OFF_P + PT_BYTES;
+  static constexpr int OFF_BAR = OFF_DS + PT_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int THREADS = 320;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
+  static constexpr uint32_t COL_DV = DQT ? 256 : 384;
+  static constexpr uint32_t COL_DK = COL_DV + (DQT ? 128 : 64);
+};
+
+enum BwdBar {
+  C_KVFULL = 0,
+  C_QFULL = 1,   // +2
+  C_QEMPTY = 3,  // +2
+  C_SFULL = 5,
+  C_DPFULL = 6,
+  C_SFREE = 7,    // 4 arrivals
+  C_DSREADY = 8,  // 4 arrivals
+  C_PFREE = 9,
+  C_DQFULL = 10,
+  C_DQFREE = 11,  // 4 arrivals
+  C_KVDONE = 12,
+  C_COUNT = 13
+};
+
+// -------------------------------------------------------------------------- pre
+// One warp per (bh, row) of the padded row range.
+__global__ void fa_bwd_pre_kernel(const __half* __restrict__ o, const __half* __restrict__ dout,
+                                  const float* __restrict__ lse, float* __restrict__ lse2,
+                                  float* __restrict__ delta, float* __restrict__ dq_acc, int S,
+                                  int H, int D, int S_pad) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  const int bh = blockIdx.y;
+  if (row >= S_pad) return;
+  const int b = bh / H, h = bh % H;
+  const size_t prow = (size_t)bh * S_pad + row;
+  float acc = 0.f;
+  if (row < S) {
+    const __half* orow = o + (((size_t)b * S + row) * H + h) * D;
+    const __half* drow = dout + (((size_t)b * S + row) * H + h) * D;
+    for (int e = lane * 2; e < D; e += 64) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(orow + e));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(drow + e));
+      acc = fmaf(a.x, c.x, acc);
+      acc = fmaf(a.y, c.y, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    delta[prow] = acc;
+    lse2[prow] = row < S ? lse[(size_t)bh * S + row] * 1.4426950408889634f
+                         : __int_as_float(0x7f800000);
+  }
+  float* qa = dq_acc + prow * D;
+  for (int e = lane * 4; e < D; e += 128) *reinterpret_cast<float4*>(qa + e) = make_float4(0, 0, 0, 0);
+}
+
+// -------------------------------------------------------------------------- post
+__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __restrict__ dq, int S,
+                                   int H, int D, int S_pad, float scale) {
+  // one thread per 8 consecutive elements of one (b, s, h) row
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = D / 8;
+  const size_t rows = (size_t)gridDim.y * S;
+  (void)rows;
+  const int bh = blockIdx.y;
+  const size_t r = idx / per_row;
+  if (r >= (size_t)S) return;
+  const int e = (int)(idx % per_row) * 8;
+  const int b = bh / H, h = bh % H;
+  const float* src = dq_acc + ((size_t)bh * S_pad + r) * D + e;
+  const float4 x0 = *reinterpret_cast<const float4*>(src);
+  const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+  uint4 w;
+  w.x = pack_half2(x0.x * scale, x0.y * scale);
+  w.y = pack_half2(x0.z * scale, x0.w * scale);
+  w.z = pack_half2(x1.x * scale, x1.y * scale);
+  w.w = pack_half2(x1.z * scale, x1.w * scale);
+  *reinterpret_cast<uint4*>(dq + (((size_t)b * S + r) * H + h) * D + e) = w;
+}
+
+// -------------------------------------------------------------------------- main
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ lse2,
+                       const float* __restrict__ delta, float* __restrict__ dq_acc,
+                       __half* __restrict__ dk, __half* __restrict__ dv, int S, int H, int S_pad,
+                       float scale, float scale_log2, int causal, int* status,
+                       unsigned long long timeout_ns) {
+  using C = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * C_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * C_COUNT + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int kv0 = kt * C::BN;
+  const int ntq = (S + C::BM - 1) / C::BM;
+  const int i0 = causal ? kv0 / C::BM : 0;  // first query tile that sees this key tile
+  const int nq = ntq - i0;
+
+  WaitCtx wc{abort_flag, status, timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C_COUNT; ++i) {
+      const uint32_t cnt = (i == C_SFREE || i == C_DSREADY || i == C_DQFREE) ? 4u : 1u;
+      mbar_init(bar(i), cnt);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_do);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(bar(C_KVFULL), 2 * C::KV_BYTES);
+      for (int a = 0; a < C::NAT; ++a) {
+        tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, h, b);
+        tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, h, b);
+      }
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % C::NST;
+        const uint32_t ph = (uint32_t)(i / C::NST) & 1u;
+        const int q0 = (i0 + i) * C::BM;
+        if (i >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
+        mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::BM * 4);
+        for (int a = 0; a < C::NAT; ++a) {
+          tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
+                      bar(C_QFULL + st), a * C::AE, q0, h, b);
+          tma_load_4d(sbase + C::OFF_DO + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_do,
+                      bar(C_QFULL + st), a * C::AE, q0, h, b);
+        }
+        bulk_load(sbase + C::OFF_LSE + st * C::BM * 4, lse2 + (size_t)bh * S_pad + q0, C::BM * 4,
+                  bar(C_QFULL + st));
+        bulk_load(sbase + C::OFF_DELTA + st * C::BM * 4, delta + (size_t)bh * S_pad + q0,
+                  C::BM * 4, bar(C_QFULL + st));
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t swz = swizzle_field(C::SWB);
+      constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false);   // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
+      constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
+                                        : make_idesc_f16(C::BM, D, true, true);  // dQ
+      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
+      for (int i = 0; ok && i < nq; ++i) {
+        const int st = i % C::NST;
+        if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc)) break;
+        if (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)) break;
+        tc_fence_after();
+        const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
+        const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
+        // S^T = K Q^T  and  dP^T = V dO^T   (M = 128 key rows, N = BM, K = D)
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int a = (kk * 16) / C::AE;
+          const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
+          const uint64_t ad = make_smem_desc(sbase + C::OFF_K + a * C::BN * C::SWB + koff, 16,
+                                             8 * C::SWB, swz);
+          const uint64_t bd = make_smem_desc(qb + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
+          mma_f16_ss(tmem + C::COL_S, ad, bd, id_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(C_SFULL));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int a = (kk * 16) / C::AE;
+          const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
+          const uint64_t ad = make_smem_desc(sbase + C::OFF_V + a * C::BN * C::SWB + koff, 16,
+                                             8 * C::SWB, swz);
+          const uint64_t bd = make_smem_desc(dob + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
+          mma_f16_ss(tmem + C::COL_DP, ad, bd, id_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(C_DPFULL));
+        if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
+        tc_fence_after();
+        // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
+#pragma unroll
+        for (int kk = 0; kk < C::BM / 16; ++kk) {
+          const int a = kk / 4;
+          const uint32_t koff = (uint32_t)(kk % 4) * 32u;
+          const uint64_t pd = make_smem_desc(sbase + C::OFF_P + a * C::BN * 128 + koff, 16, 1024, 2);
+          const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+          mma_f16_ss(tmem + C::COL_DV, pd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < C::BM / 16; ++kk) {
+          const int a = kk / 4;
+          const uint32_t koff = (uint32_t)(kk % 4) * 32u;
+          const uint64_t sd =
+              make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
+          const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+          mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (i > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(i - 1) & 1u, wc)) break;
+        tc_fence_after();
+        // dQ partial over this key tile (K = 128 key rows)
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t dsd =
+              make_smem_desc(sbase + C::OFF_DS + kk * 16 * 128, C::BN * 128, 1024, 2);
+          const uint64_t kd =
+              make_smem_desc(sbase + C::OFF_K + kk * 16 * C::SWB, C::BN * C::SWB, 8 * C::SWB, swz);
+          if constexpr (C::DQT)
+            mma_f16_ss(tmem + C::COL_DQ, kd, dsd, id_dq, kk > 0 ? 1u : 0u);  // K^T dS^T
+          else
+            mma_f16_ss(tmem + C::COL_DQ, dsd, kd, id_dq, kk > 0 ? 1u : 0u);  // dS K
+        }
+        mma_commit(bar(C_DQFULL));
+        mma_commit(bar(C_QEMPTY + st));
+        mma_commit(bar(C_PFREE));
+      }
+      mma_commit(bar(C_KVDONE));
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ softmax / dS warps
+    const int r = warp * 32 + lane;  // key row inside the tile == TMEM lane
+    const int kv_idx = kv0 + r;
+    const bool kv_ok = kv_idx < S;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int st = i % C::NST;
+      const int q0 = (i0 + i) * C::BM;
+      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc) ||
+          !mbar_wait(bar(C_SFULL), (uint32_t)i & 1u, wc) ||
+          !mbar_wait(bar(C_DPFULL), (uint32_t)i & 1u, wc) ||
+          (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lse_s = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * C::BM * 4);
+      const float* del_s = reinterpret_cast<const float*>(smem + C::OFF_DELTA + st * C::BM * 4);
+#pragma unroll 1
+      for (int c = 0; c < C::BM / 32; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::COL_S + c * 32, sr);
+        tmem_ld32(tmem + lane_base + C::COL_DP + c * 32, dr);
+        tmem_wait_ld();
+        if (c == C::BM / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_SFREE));
+        }
+        float p[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int ql = c * 32 + e;
+          const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
+          const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e]), scale_log2, -lse_s[ql])) : 0.f;
+          p[e] = pe;
+          ds[e] = pe * (__uint_as_float(dr[e]) - del_s[ql]);
+        }
+        const int a = (c * 32) / 64;
+        const int ch0 = ((c * 32) % 64) / 8;
+        const uint32_t pb = sbase + C::OFF_P + a * C::BN * 128;
+        const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = u * 8;
+          st_shared_v4(pb + sw128_offset(r, ch0 + u), pack_half2(p[e], p[e + 1]),
+                       pack_half2(p[e + 2], p[e + 3]), pack_half2(p[e + 4], p[e + 5]),
+                       pack_half2(p[e + 6], p[e + 7]));
+          st_shared_v4(sb + sw128_offset(r, ch0 + u), pack_half2(ds[e], ds[e + 1]),
+                       pack_half2(ds[e + 2], ds[e + 3]), pack_half2(ds[e + 4], ds[e + 5]),
+                       pack_half2(ds[e + 6], ds[e + 7]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_DSREADY));
+    }
+    // ------------------------------------------------------------ dK / dV epilogue
+    if (ok && mbar_wait(bar(C_KVDONE), 0, wc)) {
+      tc_fence_after();
+      __half* dvrow = dv + (((size_t)b * S + kv_idx) * H + h) * D;
+      __half* dkrow = dk + (((size_t)b * S + kv_idx) * H + h) * D;
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const uint32_t col = pass == 0 ? C::COL_DV : C::COL_DK;
+        const float f = pass == 0 ? 1.f : scale;
+        __half* dst = pass == 0 ? dvrow : dkrow;
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_base + col + c * 16, v);
+          tmem_wait_ld();
+          uint4 w0, w1;
+          w0.x = pack_half2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
+          w0.y = pack_half2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
+          w0.z = pack_half2(__uint_as_float(v[4]) * f, __uint_as_float(v[5]) * f);
+          w0.w = pack_half2(__uint_as_float(v[6]) * f, __uint_as_float(v[7]) * f);
+          w1.x = pack_half2(__uint_as_float(v[8]) * f, __uint_as_float(v[9]) * f);
+          w1.y = pack_half2(__uint_as_float(v[10]) * f, __uint_as_float(v[11]) * f);
+          w1.z = pack_half2(__uint_as_float(v[12]) * f, __uint_as_float(v[13]) * f);
+          w1.w = pack_half2(__uint_as_float(v[14]) * f, __uint_as_float(v[15]) * f);
+          if (kv_ok) {
+            reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
+            reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ epilogue warps 4..7
+    const int wq = warp - 4;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    for (int i = 0; i < nq; ++i) {
+      const int q0 = (i0 + i) * C::BM;
+      if (!mbar_wait(bar(C_DQFULL), (uint32_t)i & 1u, wc)) break;
+      tc_fence_after();
+      if constexpr (C::DQT) {
+        // TMEM lane = d, column = query row: each column is 32 consecutive d -> coalesced
+        const int d = wq * 32 + lane;
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tmem + lane_base + C::COL_DQ, v0);
+        tmem_ld32(tmem + lane_base + C::COL_DQ + 32, v1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C_DQFREE));
+        float* base = dq_acc + ((size_t)bh * S_pad + q0) * D + d;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) atomicAdd(base + (size_t)e * D, __uint_as_float(v0[e]));
+#pragma unroll
+        for (int e = 0; e < 32; ++e) atomicAdd(base + (size_t)(32 + e) * D, __uint_as_float(v1[e]));
+      } else {
+        // TMEM lane = query row, column = d
+        const int qr = wq * 32 + lane;
+        uint32_t v[D];
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t t[16];
+          tmem_ld16(tmem + lane_base + C::COL_DQ + c * 16, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[c * 16 + e] = t[e];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C_DQFREE));
+        float4* dst = reinterpret_cast<float4*>(dq_acc + ((size_t)bh * S_pad + q0 + qr) * D);
+#pragma unroll
+        for (int e = 0; e < D / 4; ++e)
+          atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                         __uint_as_float(v[4 * e + 2]),
+                                         __uint_as_float(v[4 * e + 3])));
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
+  using C = BwdCfg<D>;
+  if (cudaFuncSetAttribute(fa_bwd_main_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           C::SMEM) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  dim3 grid((a.S + C::BN - 1) / C::BN, a.B * a.H);
+  fa_bwd_main_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
+      *a.tm_q, *a.tm_do, *a.tm_k, *a.tm_v, a.lse2, a.delta, a.dq_acc, static_cast<__half*>(a.dk),
+      static_cast<__half*>(a.dv), a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f,
+      a.causal, a.status, a.timeout_ns);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int bwd_q_rows(int D) { return D == 128 ? 64 : 128; }
+
+int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
+  if (phase < 0 || phase == 0) {
+    dim3 grid((a.S_pad + 7) / 8, a.B * a.H);
+    fa_bwd_pre_kernel<<<grid, 256, 0, stream>>>(
+        static_cast<const __half*>(a.o), static_cast<const __half*>(a.dout), a.lse, a.lse2,
+        a.delta, a.dq_acc, a.S, a.H, a.D, a.S_pad);
+    if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+  }
+  int rc = FA_OK;
+  if (phase < 0 || phase == 1) switch (a.D) {
+    case 16: rc = launch_bwd_main<16>(a, stream); break;
+    case 32: rc = launch_bwd_main<32>(a, stream); break;
+    case 64: rc = launch_bwd_main<64>(a, stream); break;
+    case 128: rc = launch_bwd_main<128>(a, stream); break;
+    default: return FA_ERR_ARG;
+  }
+  if (rc != FA_OK) return rc;
+  if (phase < 0 || phase == 2) {
+    const int per_row = a.D / 8;
+    const size_t n = (size_t)a.S * per_row;
+    dim3 grid((unsigned)((n + 255) / 256), a.B * a.H);
+    fa_bwd_post_kernel<<<grid, 256, 0, stream>>>(a.dq_acc, static_cast<__half*>(a.dq), a.S, a.H,
+                                                 a.D, a.S_pad, a.scale);
+    if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+  }
+  return FA_OK;
+}
+
+}  // namespace fa_sm100

@@ -1,0 +1,53 @@
+// Internal launch interface between the C ABI layer (fa_api.cu) and the kernel
+// translation units.  Not part of the public ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/fa_sm100.h"
+
+namespace fa_sm100 {
+
+struct FwdArgs {
+  const CUtensorMap* tm_q;  // box rows: 128
+  const CUtensorMap* tm_k;  // box rows: 128
+  const CUtensorMap* tm_v;  // box rows: 128
+  void* o;
+  float* lse;
+  int B, S, H, D;
+  float scale;
+  int causal;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+struct BwdArgs {
+  const CUtensorMap* tm_q;   // box rows: bwd_q_rows(D)
+  const CUtensorMap* tm_do;  // box rows: bwd_q_rows(D)
+  const CUtensorMap* tm_k;   // box rows: 128
+  const CUtensorMap* tm_v;   // box rows: 128
+  const void* o;
+  const void* dout;
+  const float* lse;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* dq_acc;   // (B*H, S_pad, D) fp32
+  float* lse2;     // (B*H, S_pad) fp32, lse * log2(e), +inf in padding rows
+  float* delta;    // (B*H, S_pad) fp32
+  int B, S, H, D, S_pad;
+  float scale;
+  int causal;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+int launch_fwd(const FwdArgs& a, cudaStream_t stream);
+// phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion
+int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase);
+int bwd_q_rows(int D);  // query rows per backward iteration
+constexpr int kSeqPad = 128;
+
+}  // namespace fa_sm100

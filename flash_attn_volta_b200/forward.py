@@ -1,0 +1,82 @@
+"""Attention forward entry point (drop-in for flash_attn_volta/triton_fa.py:291-401).
+
+`flash_attn_forward` keeps the reference's signature, its AssertionError input
+checks (triton_fa.py:313-317), default scale (:319-320) and return convention
+(out, or (out, lse) with lse (B, H, N) fp32 natural log, +inf on fully masked
+rows).  The work runs in the sm_100a kernel behind fa_sm100_fwd; there is no
+padding of small head dims and no permute copy: the kernel reads the
+(B, N, H, D) tensors directly.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+def _as_kernel_input(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous (B, N, H, D) with a 16-byte aligned base (what TMA needs)."""
+    if not t.is_contiguous() or t.data_ptr() % 16 != 0:
+        t = t.contiguous()
+        if t.data_ptr() % 16 != 0:
+            t = t.clone()
+    return t
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def flash_attn_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    sm_scale: float | None = None,
+    return_softmax_lse: bool = False,
+):
+    """FlashAttention forward on B200: fp16 in/out, fp32 accumulation.
+
+    Args:
+        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.
+        causal:  if True apply the top-left lower-triangular mask.
+        sm_scale: softmax scale (default 1/sqrt(D)).
+        return_softmax_lse: if True also return the per-row log-sum-exp.
+
+    Returns:
+        out: (B, N, H, D) fp16 contiguous; with return_softmax_lse also
+        lse: (B, H, N) fp32, natural log, +inf for fully masked rows.
+    """
+    assert q.is_cuda and k.is_cuda and v.is_cuda, "tensors must be on CUDA"
+    assert q.dtype == torch.float16 == k.dtype == v.dtype, "fp16 only"
+    assert q.shape == k.shape == v.shape, f"qkv shape mismatch {q.shape} {k.shape} {v.shape}"
+    B, N, H, D = q.shape
+    assert D in (16, 32, 64, 128), f"unsupported head_dim {D} (allowed: 16,32,64,128)"
+    assert q.device == k.device == v.device, "q, k, v must be on the same device"
+
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+
+    q, k, v = _as_kernel_input(q), _as_kernel_input(k), _as_kernel_input(v)
+    out = torch.empty((B, N, H, D), dtype=torch.float16, device=q.device)
+    lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if return_softmax_lse else None
+    if q.numel() != 0:
+        lib = _lib.load()
+        with torch.cuda.device(q.device):
+            status = _lib.status_word(q.device)
+            rc = lib.fa_sm100_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                  lse.data_ptr() if lse is not None else None,
+                                  B, N, H, D, float(sm_scale), 1 if causal else 0,
+                                  status.data_ptr(), _stream_ptr(q.device))
+        _lib.check(rc, "fa_sm100_fwd")
+        if _lib.debug_sync():
+            _lib.check_status(q.device)
+    if return_softmax_lse:
+        return out, lse
+    return out
+
+
+# Public alias kept from the reference (triton_fa.py:401)
+flash_attn_volta = flash_attn_forward

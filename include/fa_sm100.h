@@ -1,0 +1,81 @@
+/* C ABI of the B200 (sm_100a) FlashAttention library libfa_sm100.so.
+ *
+ * Plain pointers and sizes only: every tensor is a caller-owned device buffer,
+ * fp16 tensors are contiguous (batch, seqlen, nheads, head_dim) with 16-byte
+ * aligned base addresses, LSE is contiguous (batch, nheads, seqlen) fp32.
+ * `stream` is a cudaStream_t (NULL = legacy default stream).  `status` is an
+ * optional device int the kernels OR error bits into (1 = a bounded on-device
+ * wait ran out) instead of trapping; the host reads it when it wants to.
+ * Calls are asynchronous, keep no state between calls and are thread-safe.
+ *
+ * Return codes: FA_OK, or one of the FA_ERR_* values below
+ * (fa_sm100_error_string() names them).
+ */
+#ifndef FA_SM100_H
+#define FA_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_OK 0
+#define FA_ERR_ARG 1      /* bad shape, head_dim, null or misaligned pointer */
+#define FA_ERR_TMA 2      /* cuTensorMapEncodeTiled refused a tensor map */
+#define FA_ERR_LAUNCH 3   /* kernel launch failed */
+#define FA_ERR_DEVICE 4   /* current device is not sm_100 / driver entry point missing */
+#define FA_ERR_WORKSPACE 5 /* workspace missing or smaller than fa_sm100_bwd_workspace_bytes() */
+
+#define FA_SM100_ABI_VERSION 1
+
+/* Forward: out = softmax(sm_scale * q k^T [causal mask]) v, and (if lse != NULL)
+ * the natural-log log-sum-exp of each query row, +inf for a row with no
+ * unmasked key.
+ * Replaces flash_attn_volta/triton_fa.py:291-397 (flash_attn_forward with
+ * return_softmax_lse, and _run_kernel) — same math, layout and LSE convention. */
+int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                 int batch, int seqlen, int nheads, int head_dim, float sm_scale, int causal,
+                 int* status, void* stream);
+
+/* Bytes of device workspace fa_sm100_bwd needs for this shape (fp32 dQ
+ * accumulator, per-row delta and log2-scaled LSE, rows padded to 128). */
+size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim);
+
+/* Backward: given dout, the forward inputs q, k, v, its output `out` and LSE,
+ * writes dq, dk, dv (fp16, same layout as q).  `workspace` is caller-owned
+ * device memory of at least fa_sm100_bwd_workspace_bytes() bytes, 256-byte
+ * aligned; its contents need not be initialised.
+ * Replaces flash_attn_volta/triton_fa_bwd.py:587-700 (flash_attn_backward and
+ * _run_bwd_kernels: delta = rowsum(O*dO), then the dQ and dK/dV kernels). */
+int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, const void* out,
+                 const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                 size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
+                 float sm_scale, int causal, int* status, void* stream);
+
+/* The three launches fa_sm100_bwd makes, one at a time, on the same arguments:
+ * phase 0 = delta / log2-LSE preparation and zeroing of the dQ accumulator,
+ * phase 1 = the main backward kernel (dK, dV, dQ partial sums),
+ * phase 2 = dQ accumulator -> fp16 dq.  Running 0, 1, 2 in stream order equals
+ * one fa_sm100_bwd call.  For callers that schedule or time the phases apart.
+ * No counterpart in the reference (its two Triton launches are internal,
+ * triton_fa_bwd.py:667-695). */
+int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
+                       const void* out, const float* lse, void* dq, void* dk, void* dv,
+                       void* workspace, size_t workspace_bytes, int batch, int seqlen,
+                       int nheads, int head_dim, float sm_scale, int causal, int* status,
+                       void* stream);
+
+/* Upper bound, in nanoseconds, of every on-device wait of later launches
+ * (default 4e9).  Process-wide. */
+void fa_sm100_set_wait_timeout_ns(uint64_t ns);
+
+const char* fa_sm100_error_string(int code);
+int fa_sm100_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_SM100_H */

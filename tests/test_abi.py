@@ -1,0 +1,79 @@
+"""CPU tests of the C ABI library: it loads, exports what include/fa_sm100.h
+declares, and rejects bad arguments before touching a GPU."""
+import os
+import re
+
+import pytest
+import torch
+
+from flash_attn_volta_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    names = []
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            txt = open(os.path.join(ROOT, "include", fn)).read()
+            names += re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(fa_\w+)\s*\(", txt, re.M)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared_functions()
+    assert "fa_sm100_fwd" in names and "fa_sm100_bwd" in names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    assert lib.fa_sm100_abi_version() == 1
+
+
+def test_error_strings():
+    lib = _lib.load()
+    for code in range(6):
+        assert lib.fa_sm100_error_string(code)
+
+
+@pytest.mark.parametrize("shape", [(0, 16, 1, 64), (1, 0, 1, 64), (1, 16, 0, 64),
+                                   (1, 16, 1, 48), (1, 16, 1, 256)])
+def test_fwd_rejects_bad_shapes(shape):
+    lib = _lib.load()
+    B, S, H, D = shape
+    rc = lib.fa_sm100_fwd(16, 16, 16, 16, None, B, S, H, D, 1.0, 0, None, None)
+    assert rc == _lib.FA_ERR_ARG
+
+
+def test_fwd_rejects_null_and_misaligned():
+    lib = _lib.load()
+    assert lib.fa_sm100_fwd(None, 16, 16, 16, None, 1, 16, 1, 64, 1.0, 0, None, None) == 1
+    assert lib.fa_sm100_fwd(16, 18, 16, 16, None, 1, 16, 1, 64, 1.0, 0, None, None) == 1
+
+
+def test_bwd_workspace_contract():
+    lib = _lib.load()
+    n = lib.fa_sm100_bwd_workspace_bytes(2, 100, 3, 64)
+    rows = 2 * 3 * 128  # rows padded to 128
+    assert n >= rows * 64 * 4 + 2 * rows * 4
+    assert lib.fa_sm100_bwd_workspace_bytes(1, 1, 1, 48) == 0
+    # too-small workspace is reported before any device work
+    rc = lib.fa_sm100_bwd(16, 16, 16, 16, 16, 16, 16, 16, 16, 256, n - 1, 2, 100, 3, 64, 1.0, 0,
+                          None, None)
+    assert rc == _lib.FA_ERR_WORKSPACE
+
+
+def test_python_api_asserts_like_reference():
+    from flash_attn_volta_b200 import flash_attn_backward, flash_attn_forward
+    q = torch.zeros(1, 8, 1, 64, dtype=torch.float16)
+    with pytest.raises(AssertionError):
+        flash_attn_forward(q, q, q)
+    with pytest.raises(AssertionError):
+        flash_attn_backward(q, q, q, q, q, torch.zeros(1, 1, 8))
+
+
+def test_public_api_surface():
+    import flash_attn_volta_b200 as m
+    assert m.__version__ == "0.2.0"
+    assert set(m.__all__) == {"flash_attn_forward", "flash_attn_volta", "flash_attn_backward",
+                              "flash_attn"}
+    assert m.flash_attn_volta is m.flash_attn_forward

@@ -6,6 +6,8 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -35,10 +37,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// The current device must be compute capability 10.0 (B200 / sm_100a).
+// The current device must be compute capability 10.0 (B200 / sm_100a).  Also
+// makes the device's primary context current in the calling thread (a thread
+// that has only made runtime calls that do not bind a context, such as torch's
+// autograd worker, has none, and the driver-level tensor-map encoder then
+// fails with CUDA_ERROR_INVALID_CONTEXT).
 int check_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_DEVICE;
+  if (cudaSetDevice(dev) != cudaSuccess) return FA_ERR_DEVICE;
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
@@ -70,6 +77,13 @@ int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, i
   const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS && std::getenv("FA_SM100_DEBUG")) {
+    std::fprintf(stderr,
+                 "fa_sm100: cuTensorMapEncodeTiled failed (CUresult %d) ptr=%p dims={%d,%d,%d,%d} "
+                 "strides={%llu,%llu,%llu} box={%u,%u,1,1}\n",
+                 (int)r, ptr, D, S, H, B, (unsigned long long)strides[0],
+                 (unsigned long long)strides[1], (unsigned long long)strides[2], box[0], box[1]);
+  }
   return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TMA;
 }
 

@@ -19,6 +19,7 @@ FA_ERR_TMA = 2
 FA_ERR_LAUNCH = 3
 FA_ERR_DEVICE = 4
 FA_ERR_WORKSPACE = 5
+FA_ERR_SCRATCH_LIMIT = 6
 
 STATUS_TIMEOUT = 1
 
@@ -50,6 +51,9 @@ def load() -> ctypes.CDLL:
             lib.fa_sm100_bwd.restype = _c_int
             lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes
             lib.fa_sm100_bwd_phase.restype = _c_int
+            lib.fa_sm100_bwd_noalloc.argtypes = [_vp] * 9 + [_c_int] * 4 + [_c_float, _c_int,
+                                                                             _vp, _vp]
+            lib.fa_sm100_bwd_noalloc.restype = _c_int
             lib.fa_sm100_bwd_workspace_bytes.argtypes = [_c_int, _c_int, _c_int, _c_int]
             lib.fa_sm100_bwd_workspace_bytes.restype = _c_size
             lib.fa_sm100_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]

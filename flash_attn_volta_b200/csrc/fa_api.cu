@@ -121,6 +121,8 @@ const char* fa_sm100_error_string(int code) {
     case FA_ERR_LAUNCH: return "kernel launch failed";
     case FA_ERR_DEVICE: return "current device is not sm_100 or the driver entry point is missing";
     case FA_ERR_WORKSPACE: return "workspace missing or too small";
+    case FA_ERR_SCRATCH_LIMIT:
+      return "shape needs more scratch than the static array of fa_sm100_bwd_noalloc (32 MiB)";
     default: return "unknown error";
   }
 }
@@ -162,10 +164,13 @@ size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_
   return ws_layout(batch, seqlen, nheads, head_dim).total;
 }
 
-static int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
-                    const void* out, const float* lse, void* dq, void* dk, void* dv,
-                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
-                    int head_dim, float sm_scale, int causal, int* status, void* stream) {
+}  // extern "C"
+
+int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k,
+                              const void* v, const void* out, const float* lse, void* dq, void* dk,
+                              void* dv, void* workspace, size_t workspace_bytes, int batch, int seqlen,
+                              int nheads, int head_dim, float sm_scale, int causal, int* status,
+                              void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
   const void* ptrs[] = {dout, q, k, v, out, dq, dk, dv};
   for (const void* p : ptrs)
@@ -208,6 +213,8 @@ static int bwd_impl(int phase, const void* dout, const void* q, const void* k, c
   a.timeout_ns = g_timeout_ns.load();
   return launch_bwd(a, static_cast<cudaStream_t>(stream), phase);
 }
+
+extern "C" {
 
 int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, const void* out,
                  const float* lse, void* dq, void* dk, void* dv, void* workspace,

@@ -47,7 +47,14 @@ struct BwdArgs {
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 // phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion
 int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase);
-int bwd_q_rows(int D);  // query rows per backward iteration
+int bwd_q_rows(int D);
+
+// Argument checks, tensor maps and launches of the backward on a caller-given
+// workspace (phase as in launch_bwd).  Shared by the C ABI entry points.
+int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
+             const void* out, const float* lse, void* dq, void* dk, void* dv, void* workspace,
+             size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
+             float sm_scale, int causal, int* status, void* stream);  // query rows per backward iteration
 constexpr int kSeqPad = 128;
 
 }  // namespace fa_sm100

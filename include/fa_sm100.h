@@ -27,6 +27,10 @@ extern "C" {
 #define FA_ERR_LAUNCH 3   /* kernel launch failed */
 #define FA_ERR_DEVICE 4   /* current device is not sm_100 / driver entry point missing */
 #define FA_ERR_WORKSPACE 5 /* workspace missing or smaller than fa_sm100_bwd_workspace_bytes() */
+#define FA_ERR_SCRATCH_LIMIT 6 /* shape needs more than FA_SM100_NOALLOC_SCRATCH_BYTES */
+
+/* Size of the static device scratch array behind fa_sm100_bwd_noalloc. */
+#define FA_SM100_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 #define FA_SM100_ABI_VERSION 1
 
@@ -66,6 +70,24 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
                        void* workspace, size_t workspace_bytes, int batch, int seqlen,
                        int nheads, int head_dim, float sm_scale, int causal, int* status,
                        void* stream);
+
+/* Backward that allocates nothing, for callers that cannot allocate device
+ * memory when they run it (pre-planned buffer pools, execution phases where
+ * allocation is forbidden, fixed memory budgets).  Same arguments and results
+ * as fa_sm100_bwd, minus the workspace: the scratch it needs (the same bytes
+ * fa_sm100_bwd_workspace_bytes() reports) lives in one static device array of
+ * FA_SM100_NOALLOC_SCRATCH_BYTES (32 MiB) per GPU, held from library load
+ * until process exit.  Shapes that need more return FA_ERR_SCRATCH_LIMIT
+ * (e.g. head_dim 128 fits at most about 63k padded rows batch*nheads*seqlen).
+ * The first call on a device looks up the array's device address (with that
+ * device current); make it before any stream capture.  All calls share the
+ * array, so calls that overlap on the GPU race; inputs and outputs are still
+ * caller-owned.  It calls no cudaMalloc / cudaFree.
+ * No counterpart in the reference. */
+int fa_sm100_bwd_noalloc(const void* dout, const void* q, const void* k, const void* v,
+                         const void* out, const float* lse, void* dq, void* dk, void* dv,
+                         int batch, int seqlen, int nheads, int head_dim, float sm_scale,
+                         int causal, int* status, void* stream);
 
 /* Upper bound, in nanoseconds, of every on-device wait of later launches
  * (default 4e9).  Process-wide. */

@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_error_strings():
     lib = _lib.load()
-    for code in range(6):
+    for code in range(7):
         assert lib.fa_sm100_error_string(code)
 
 

@@ -13,15 +13,19 @@
 //   fa_bwd_pre   delta (fp32), LSE * log2(e), zero the dQ accumulator.
 //   fa_bwd_main  one CTA = one 128-row key/value tile of one (batch, head);
 //                loops over query tiles of BM rows (64 for D=128, else 128).
-//     warps 0-3  "softmax": thread r owns key row r.  Reads S^T and dP^T from
-//                tensor memory, P^T = exp2(S^T*scale*log2e - LSE2),
-//                dS^T = P^T (dP^T - delta), writes both (fp16) to shared memory;
-//                final dK/dV epilogue.
-//     warps 4-7  dQ epilogue: read this tile's dQ partial from tensor memory and
-//                add it into the fp32 accumulator (global reductions).
-//     warp 8     TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
-//     warp 9     MMA issuer: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO,
-//                dK += dS^T Q, dQ partial = dS K (stored transposed for D=128).
+//     warps 0-7  "softmax": warp w owns key rows 32*(w%4).. (its TMEM lane
+//                quarter) and half of the query columns.  Loads S^T and dP^T
+//                from tensor memory into registers and releases them at once
+//                (so the next tile's S^T / dP^T MMAs run while it computes),
+//                P^T = exp2(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - delta),
+//                writes both (fp16) to shared memory; final dK/dV epilogue.
+//     warps 8-11 dQ epilogue: read this tile's dQ partial from tensor memory,
+//                stage it in shared memory and add it into the fp32 accumulator
+//                with one bulk reduction (cp.reduce.async.bulk .add.f32).
+//     warp 12    TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
+//     warp 13    MMA issuer: S^T = K Q^T, dP^T = V dO^T (next tile, issued
+//                early), then dV += P^T dO, dK += dS^T Q, dQ partial = dS K
+//                (stored transposed for D=128).
 //   fa_bwd_post  dQ = fp16(scale * accumulator) in (B, S, H, D).
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -52,9 +56,12 @@ struct BwdCfg {
   static constexpr int OFF_DELTA = OFF_LSE + NST * BM * 4;
   static constexpr int OFF_P = ((OFF_DELTA + NST * BM * 4) + 1023) / 1024 * 1024;
   static constexpr int OFF_DS = OFF_P + PT_BYTES;
-  static constexpr int OFF_BAR = OFF_DS + PT_BYTES;
+  static constexpr int DQ_STAGE_BYTES = BM * D * 4;  // one dQ partial, [q][d] fp32
+  static constexpr int NDQ = (D == 64) ? 1 : 2;        // dQ staging buffers
+  static constexpr int OFF_DQS = OFF_DS + PT_BYTES;
+  static constexpr int OFF_BAR = OFF_DQS + NDQ * DQ_STAGE_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 448;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
   static constexpr uint32_t COL_DV = DQT ? 256 : 384;
@@ -67,8 +74,8 @@ enum BwdBar {
   C_QEMPTY = 3,  // +2
   C_SFULL = 5,
   C_DPFULL = 6,
-  C_SFREE = 7,    // 4 arrivals
-  C_DSREADY = 8,  // 4 arrivals
+  C_SFREE = 7,    // 8 arrivals (softmax warps hold S^T / dP^T in registers)
+  C_DSREADY = 8,  // 8 arrivals (P^T / dS^T written to shared memory)
   C_PFREE = 9,
   C_DQFULL = 10,
   C_DQFREE = 11,  // 4 arrivals
@@ -136,7 +143,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __r
 
 // -------------------------------------------------------------------------- main
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -146,6 +153,7 @@ __global__ void __launch_bounds__(320, 1)
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
   using C = BwdCfg<D>;
+  constexpr int HW = C::BM / 2;  // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -168,13 +176,15 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C_COUNT; ++i) {
-      const uint32_t cnt = (i == C_SFREE || i == C_DSREADY || i == C_DQFREE) ? 4u : 1u;
+      uint32_t cnt = 1;
+      if (i == C_SFREE || i == C_DSREADY) cnt = 8;
+      if (i == C_DQFREE) cnt = 4;
       mbar_init(bar(i), cnt);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -183,7 +193,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(320, 1)
                   C::BM * 4, bar(C_QFULL + st));
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
@@ -221,15 +231,11 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
       constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
                                         : make_idesc_f16(C::BM, D, true, true);  // dQ
-      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
-      for (int i = 0; ok && i < nq; ++i) {
+      // S^T = K Q^T and dP^T = V dO^T for query tile i (M = 128 key rows, N = BM, K = D)
+      auto issue_s_dp = [&](int i) {
         const int st = i % C::NST;
-        if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc)) break;
-        if (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)) break;
-        tc_fence_after();
         const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
-        // S^T = K Q^T  and  dP^T = V dO^T   (M = 128 key rows, N = BM, K = D)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int a = (kk * 16) / C::AE;
@@ -239,7 +245,6 @@ __global__ void __launch_bounds__(320, 1)
           const uint64_t bd = make_smem_desc(qb + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
           mma_f16_ss(tmem + C::COL_S, ad, bd, id_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(C_SFULL));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int a = (kk * 16) / C::AE;
@@ -249,9 +254,28 @@ __global__ void __launch_bounds__(320, 1)
           const uint64_t bd = make_smem_desc(dob + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
           mma_f16_ss(tmem + C::COL_DP, ad, bd, id_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(C_DPFULL));
+        mma_commit(bar(C_SFULL));
+      };
+      bool ok = mbar_wait(bar(C_KVFULL), 0, wc) && (nq <= 0 || mbar_wait(bar(C_QFULL), 0, wc));
+      if (ok && nq > 0) {
+        tc_fence_after();
+        issue_s_dp(0);
+      }
+      for (int i = 0; ok && i < nq; ++i) {
+        const int st = i % C::NST;
+        // Next tile's S^T / dP^T as soon as the softmax warps hold this tile's in registers.
+        if (i + 1 < nq) {
+          const int st1 = (i + 1) % C::NST;
+          if (!mbar_wait(bar(C_QFULL + st1), (uint32_t)((i + 1) / C::NST) & 1u, wc) ||
+              !mbar_wait(bar(C_SFREE), (uint32_t)i & 1u, wc))
+            break;
+          tc_fence_after();
+          issue_s_dp(i + 1);
+        }
         if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
         tc_fence_after();
+        const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
+        const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
         // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
 #pragma unroll
         for (int kk = 0; kk < C::BM / 16; ++kk) {
@@ -290,77 +314,89 @@ __global__ void __launch_bounds__(320, 1)
       }
       mma_commit(bar(C_KVDONE));
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------------ softmax / dS warps
-    const int r = warp * 32 + lane;  // key row inside the tile == TMEM lane
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax / dS warps 0..7
+    const int lq = warp & 3;         // TMEM lane quarter
+    const int hf = warp >> 2;        // which half of the query columns
+    const int r = lq * 32 + lane;    // key row inside the tile == TMEM lane
     const int kv_idx = kv0 + r;
     const bool kv_ok = kv_idx < S;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+    const int c0 = hf * HW;          // first query column of this thread
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       const int st = i % C::NST;
       const int q0 = (i0 + i) * C::BM;
       if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc) ||
-          !mbar_wait(bar(C_SFULL), (uint32_t)i & 1u, wc) ||
-          !mbar_wait(bar(C_DPFULL), (uint32_t)i & 1u, wc) ||
-          (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc))) {
+          !mbar_wait(bar(C_SFULL), (uint32_t)i & 1u, wc)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      uint32_t sr[HW], dr[HW];
+#pragma unroll
+      for (int c = 0; c < HW / 32; ++c) {
+        tmem_ld32(tmem + lane_base + C::COL_S + c0 + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+        tmem_ld32(tmem + lane_base + C::COL_DP + c0 + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&dr[c * 32]));
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_SFREE));
       const float* lse_s = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * C::BM * 4);
       const float* del_s = reinterpret_cast<const float*>(smem + C::OFF_DELTA + st * C::BM * 4);
-#pragma unroll 1
-      for (int c = 0; c < C::BM / 32; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::COL_S + c * 32, sr);
-        tmem_ld32(tmem + lane_base + C::COL_DP + c * 32, dr);
-        tmem_wait_ld();
-        if (c == C::BM / 32 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(C_SFREE));
-        }
-        float p[32], ds[32];
+      // P^T and dS^T for this thread's HW query columns, packed to fp16 pairs in place
+      uint32_t pp[HW / 2], dd[HW / 2];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int ql = c * 32 + e;
+      for (int e = 0; e < HW; e += 2) {
+        float p2[2], d2[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int ql = c0 + e + u;
           const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
-          const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e]), scale_log2, -lse_s[ql])) : 0.f;
-          p[e] = pe;
-          ds[e] = pe * (__uint_as_float(dr[e]) - del_s[ql]);
+          const float pe =
+              valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lse_s[ql])) : 0.f;
+          p2[u] = pe;
+          d2[u] = pe * (__uint_as_float(dr[e + u]) - del_s[ql]);
         }
-        const int a = (c * 32) / 64;
-        const int ch0 = ((c * 32) % 64) / 8;
-        const uint32_t pb = sbase + C::OFF_P + a * C::BN * 128;
-        const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+        pp[e / 2] = pack_half2(p2[0], p2[1]);
+        dd[e / 2] = pack_half2(d2[0], d2[1]);
+      }
+      if (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc)) {
+        ok = false;
+        break;
+      }
+      // Write to the [key row][query col] K-major SW128 tiles (64-column atoms)
+      const int a = c0 / 64;
+      const int ch0 = (c0 % 64) / 8;
+      const uint32_t pb = sbase + C::OFF_P + a * C::BN * 128;
+      const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = u * 8;
-          st_shared_v4(pb + sw128_offset(r, ch0 + u), pack_half2(p[e], p[e + 1]),
-                       pack_half2(p[e + 2], p[e + 3]), pack_half2(p[e + 4], p[e + 5]),
-                       pack_half2(p[e + 6], p[e + 7]));
-          st_shared_v4(sb + sw128_offset(r, ch0 + u), pack_half2(ds[e], ds[e + 1]),
-                       pack_half2(ds[e + 2], ds[e + 3]), pack_half2(ds[e + 4], ds[e + 5]),
-                       pack_half2(ds[e + 6], ds[e + 7]));
-        }
+      for (int u = 0; u < HW / 8; ++u) {
+        st_shared_v4(pb + sw128_offset(r, ch0 + u), pp[4 * u], pp[4 * u + 1], pp[4 * u + 2],
+                     pp[4 * u + 3]);
+        st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
+                     dd[4 * u + 3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C_DSREADY));
     }
     // ------------------------------------------------------------ dK / dV epilogue
-    if (ok && mbar_wait(bar(C_KVDONE), 0, wc)) {
+    constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
+    if (ok && hf * EC < D && mbar_wait(bar(C_KVDONE), 0, wc)) {
       tc_fence_after();
       __half* dvrow = dv + (((size_t)b * S + kv_idx) * H + h) * D;
       __half* dkrow = dk + (((size_t)b * S + kv_idx) * H + h) * D;
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
-        const uint32_t col = pass == 0 ? C::COL_DV : C::COL_DK;
+        const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
         const float f = pass == 0 ? 1.f : scale;
-        __half* dst = pass == 0 ? dvrow : dkrow;
+        __half* dst = (pass == 0 ? dvrow : dkrow) + hf * EC;
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
+        for (int c = 0; c < EC / 16; ++c) {
           uint32_t v[16];
           tmem_ld16(tmem + lane_base + col + c * 16, v);
           tmem_wait_ld();
@@ -380,16 +416,21 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
-  } else {
-    // ------------------------------------------------------------ dQ epilogue warps 4..7
-    const int wq = warp - 4;
+  } else if (warp < 12) {
+    // ------------------------------------------------------------ dQ epilogue warps 8..11
+    // Each tile's dQ partial goes TMEM -> registers -> shared memory ([q][d] fp32,
+    // the accumulator's own layout) -> one bulk fp32 reduction into global memory.
+    const int wq = warp - 8;
+    const int tid = threadIdx.x - 256;  // 0..127
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     for (int i = 0; i < nq; ++i) {
       const int q0 = (i0 + i) * C::BM;
+      const int sbuf = i % C::NDQ;
+      const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
       if (!mbar_wait(bar(C_DQFULL), (uint32_t)i & 1u, wc)) break;
       tc_fence_after();
       if constexpr (C::DQT) {
-        // TMEM lane = d, column = query row: each column is 32 consecutive d -> coalesced
+        // TMEM lane = d, column = query row
         const int d = wq * 32 + lane;
         uint32_t v0[32], v1[32];
         tmem_ld32(tmem + lane_base + C::COL_DQ, v0);
@@ -398,40 +439,54 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_DQFREE));
-        float* base = dq_acc + ((size_t)bh * S_pad + q0) * D + d;
+        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
+        named_bar_sync(1, 128);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) atomicAdd(base + (size_t)e * D, __uint_as_float(v0[e]));
+        for (int e = 0; e < 32; ++e) st_shared_f32(stage + (uint32_t)(e * D + d) * 4u, __uint_as_float(v0[e]));
 #pragma unroll
-        for (int e = 0; e < 32; ++e) atomicAdd(base + (size_t)(32 + e) * D, __uint_as_float(v1[e]));
+        for (int e = 0; e < 32; ++e)
+          st_shared_f32(stage + (uint32_t)((32 + e) * D + d) * 4u, __uint_as_float(v1[e]));
       } else {
         // TMEM lane = query row, column = d
         const int qr = wq * 32 + lane;
         uint32_t v[D];
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
-          uint32_t t[16];
-          tmem_ld16(tmem + lane_base + C::COL_DQ + c * 16, t);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) v[c * 16 + e] = t[e];
+          tmem_ld16(tmem + lane_base + C::COL_DQ + c * 16,
+                    *reinterpret_cast<uint32_t(*)[16]>(&v[c * 16]));
         }
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_DQFREE));
-        float4* dst = reinterpret_cast<float4*>(dq_acc + ((size_t)bh * S_pad + q0 + qr) * D);
+        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();
+        named_bar_sync(1, 128);
+        const uint32_t rowa = stage + (uint32_t)(qr * D * 4);
 #pragma unroll
-        for (int e = 0; e < D / 4; ++e)
-          atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                         __uint_as_float(v[4 * e + 2]),
-                                         __uint_as_float(v[4 * e + 3])));
+        for (int c = 0; c < D / 4; ++c) {
+          const int cc = (c + lane) % (D / 4);  // rotate chunks across lanes: no bank conflicts
+          uint32_t w0 = v[4 * c], w1 = v[4 * c + 1], w2 = v[4 * c + 2], w3 = v[4 * c + 3];
+          // select the rotated chunk without dynamic register indexing
+#pragma unroll
+          for (int t = 0; t < D / 4; ++t)
+            if (t == cc) { w0 = v[4 * t]; w1 = v[4 * t + 1]; w2 = v[4 * t + 2]; w3 = v[4 * t + 3]; }
+          st_shared_v4(rowa + (uint32_t)cc * 16u, w0, w1, w2, w3);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (tid == 0) {
+        bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
+        bulk_commit_group();
       }
     }
+    if (tid == 0) bulk_wait_group_all();
   }
 
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

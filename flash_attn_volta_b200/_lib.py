@@ -36,7 +36,7 @@ def load() -> ctypes.CDLL:
         return _lib
     with _lock:
         if _lib is None:
-            path = lib_path()
+            path = os.environ.get("FA_SM100_LIB") or lib_path()
             if not os.path.exists(path):
                 raise RuntimeError(
                     f"{path} is missing: build it with `python -m flash_attn_volta_b200.build` "

@@ -44,7 +44,7 @@ struct BwdCfg {
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;
   static constexpr int AE = SWB / 2;
   static constexpr int NAT = D / AE;
-  static constexpr int NST = 2;
+  static constexpr int NST = (D == 64) ? 2 : 3;  // Q / dO / LSE2 / delta ring depth
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int PT_BYTES = BN * BM * 2;  // [key row][query col], 64-col atoms
@@ -54,13 +54,14 @@ struct BwdCfg {
   static constexpr int OFF_DO = OFF_Q + NST * Q_BYTES;
   static constexpr int OFF_LSE = OFF_DO + NST * Q_BYTES;
   static constexpr int OFF_DELTA = OFF_LSE + NST * BM * 4;
-  static constexpr int OFF_P = ((OFF_DELTA + NST * BM * 4) + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = OFF_DELTA + NST * BM * 4;  // barriers, TMEM slot, abort flag
+  static constexpr int OFF_P = ((OFF_BAR + 256) + 1023) / 1024 * 1024;
   static constexpr int OFF_DS = OFF_P + PT_BYTES;
   static constexpr int DQ_STAGE_BYTES = BM * D * 4;  // one dQ partial, [q][d] fp32
-  static constexpr int NDQ = (D == 64) ? 1 : 2;        // dQ staging buffers
+  static constexpr int NDQ = (D <= 32) ? 2 : 1;        // dQ staging buffers
   static constexpr int OFF_DQS = OFF_DS + PT_BYTES;
-  static constexpr int OFF_BAR = OFF_DQS + NDQ * DQ_STAGE_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int SMEM = OFF_DQS + NDQ * DQ_STAGE_BYTES + 1024;  // + alignment slack
+  static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr int THREADS = 448;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
@@ -70,17 +71,17 @@ struct BwdCfg {
 
 enum BwdBar {
   C_KVFULL = 0,
-  C_QFULL = 1,   // +2
-  C_QEMPTY = 3,  // +2
-  C_SFULL = 5,
-  C_DPFULL = 6,
-  C_SFREE = 7,    // 8 arrivals (softmax warps hold S^T / dP^T in registers)
-  C_DSREADY = 8,  // 8 arrivals (P^T / dS^T written to shared memory)
-  C_PFREE = 9,
-  C_DQFULL = 10,
-  C_DQFREE = 11,  // 4 arrivals
-  C_KVDONE = 12,
-  C_COUNT = 13
+  C_QFULL = 1,   // +NST (<= 3)
+  C_QEMPTY = 4,  // +NST
+  C_SFULL = 7,
+  C_DPFULL = 8,
+  C_SFREE = 9,     // 8 arrivals (softmax warps hold S^T / dP^T in registers)
+  C_DSREADY = 10,  // 8 arrivals (P^T / dS^T written to shared memory)
+  C_PFREE = 11,
+  C_DQFULL = 12,
+  C_DQFREE = 13,  // 4 arrivals
+  C_KVDONE = 14,
+  C_COUNT = 15
 };
 
 // -------------------------------------------------------------------------- pre
@@ -441,6 +442,9 @@ __global__ void __launch_bounds__(448, 1)
         if (lane == 0) mbar_arrive(bar(C_DQFREE));
         if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
         named_bar_sync(1, 128);
+#if defined(FA_BWD_EXPERIMENT) && FA_BWD_EXPERIMENT == 2
+        if (d < 0)
+#endif
 #pragma unroll
         for (int e = 0; e < 32; ++e) st_shared_f32(stage + (uint32_t)(e * D + d) * 4u, __uint_as_float(v0[e]));
 #pragma unroll
@@ -476,7 +480,9 @@ __global__ void __launch_bounds__(448, 1)
       fence_proxy_async_smem();
       named_bar_sync(1, 128);
       if (tid == 0) {
+#if !defined(FA_BWD_EXPERIMENT) || FA_BWD_EXPERIMENT == 0
         bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
+#endif
         bulk_commit_group();
       }
     }

@@ -17,14 +17,17 @@
 //                quarter) and half of the query columns.  Loads S^T and dP^T
 //                from tensor memory into registers and releases them at once
 //                (so the next tile's S^T / dP^T MMAs run while it computes),
-//                P^T = exp2(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - delta),
-//                writes both (fp16) to shared memory; final dK/dV epilogue.
+//                P^T = exp2(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - delta);
+//                P^T (fp16) goes to tensor memory as the A operand of dV += P^T dO,
+//                dS^T to shared memory (for dQ) and, for D=128, to tensor memory
+//                too (A operand of dK += dS^T Q); final dK/dV epilogue.
 //     warps 8-11 dQ epilogue: read this tile's dQ partial from tensor memory,
 //                stage it in shared memory and add it into the fp32 accumulator
 //                with one bulk reduction (cp.reduce.async.bulk .add.f32).
 //     warp 12    TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
-//     warp 13    MMA issuer: S^T = K Q^T, dP^T = V dO^T (next tile, issued
-//                early), then dV += P^T dO, dK += dS^T Q, dQ partial = dS K
+//     warp 13    MMA issuer A: S^T = K Q^T, dP^T = V dO^T of each tile, issued
+//                as soon as the previous tile's S^T / dP^T are in registers.
+//     warp 14    MMA issuer B: dV += P^T dO, dK += dS^T Q, dQ partial = dS K
 //                (stored transposed for D=128).
 //   fa_bwd_post  dQ = fp16(scale * accumulator) in (B, S, H, D).
 #include <cuda.h>
@@ -36,6 +39,18 @@
 
 namespace fa_sm100 {
 
+#ifdef FA_BWD_TRACE
+__device__ unsigned long long g_trace[64][16];
+#define TRACE(slot, it)                                                              \
+  do {                                                                               \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (it) < 64) g_trace[it][slot] = clock64(); \
+  } while (0)
+#else
+#define TRACE(slot, it) \
+  do {                  \
+  } while (0)
+#endif
+
 template <int D>
 struct BwdCfg {
   static constexpr int BN = 128;                    // key rows per CTA
@@ -44,7 +59,7 @@ struct BwdCfg {
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;
   static constexpr int AE = SWB / 2;
   static constexpr int NAT = D / AE;
-  static constexpr int NST = (D == 64) ? 2 : 3;  // Q / dO / LSE2 / delta ring depth
+  static constexpr int NST = 3;  // Q / dO / LSE2 / delta ring depth
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int PT_BYTES = BN * BM * 2;  // [key row][query col], 64-col atoms
@@ -56,17 +71,23 @@ struct BwdCfg {
   static constexpr int OFF_DELTA = OFF_LSE + NST * BM * 4;
   static constexpr int OFF_BAR = OFF_DELTA + NST * BM * 4;  // barriers, TMEM slot, abort flag
   static constexpr int OFF_P = ((OFF_BAR + 256) + 1023) / 1024 * 1024;
-  static constexpr int OFF_DS = OFF_P + PT_BYTES;
+  static constexpr int OFF_DS = OFF_P;  // P^T lives in tensor memory, not here
   static constexpr int DQ_STAGE_BYTES = BM * D * 4;  // one dQ partial, [q][d] fp32
   static constexpr int NDQ = (D <= 32) ? 2 : 1;        // dQ staging buffers
   static constexpr int OFF_DQS = OFF_DS + PT_BYTES;
   static constexpr int SMEM = OFF_DQS + NDQ * DQ_STAGE_BYTES + 1024;  // + alignment slack
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 480;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
   static constexpr uint32_t COL_DV = DQT ? 256 : 384;
   static constexpr uint32_t COL_DK = COL_DV + (DQT ? 128 : 64);
+  // P^T (fp16 pairs, BM/2 columns) in tensor memory: A operand of dV += P^T dO.
+  static constexpr uint32_t COL_PT = DQT ? 192 : 320;
+  // D=128 also keeps dS^T there (A operand of dK += dS^T Q); it goes to shared
+  // memory as well, where dQ reads it.
+  static constexpr bool DS_TMEM = DQT;
+  static constexpr uint32_t COL_DST = 224;
 };
 
 enum BwdBar {
@@ -144,7 +165,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __r
 
 // -------------------------------------------------------------------------- main
 template <int D>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(480, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -210,7 +231,9 @@ __global__ void __launch_bounds__(448, 1)
         const int st = i % C::NST;
         const uint32_t ph = (uint32_t)(i / C::NST) & 1u;
         const int q0 = (i0 + i) * C::BM;
+        TRACE(0, i);
         if (i >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
+        TRACE(1, i);
         mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::BM * 4);
         for (int a = 0; a < C::NAT; ++a) {
           tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
@@ -225,13 +248,10 @@ __global__ void __launch_bounds__(448, 1)
       }
     }
   } else if (warp == 13) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuer A
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
       constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false);   // S^T, dP^T
-      constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
-      constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
-                                        : make_idesc_f16(C::BM, D, true, true);  // dQ
       // S^T = K Q^T and dP^T = V dO^T for query tile i (M = 128 key rows, N = BM, K = D)
       auto issue_s_dp = [&](int i) {
         const int st = i % C::NST;
@@ -257,45 +277,62 @@ __global__ void __launch_bounds__(448, 1)
         }
         mma_commit(bar(C_SFULL));
       };
-      bool ok = mbar_wait(bar(C_KVFULL), 0, wc) && (nq <= 0 || mbar_wait(bar(C_QFULL), 0, wc));
-      if (ok && nq > 0) {
+      // Issuer A (warp 13): S^T / dP^T of every query tile, each as soon as the
+      // softmax warps hold the previous tile's values in registers.
+      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
+      for (int i = 0; ok && i < nq; ++i) {
+        if (!mbar_wait(bar(C_QFULL + i % C::NST), (uint32_t)(i / C::NST) & 1u, wc) ||
+            (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)))
+          break;
+        TRACE(2, i);
         tc_fence_after();
-        issue_s_dp(0);
+        issue_s_dp(i);
+        TRACE(3, i);
       }
+    }
+  } else if (warp == 14) {
+    // ------------------------------------------------------------ MMA issuer B
+    // dV, dK and the dQ partial of each tile once its P^T / dS^T are ready.  A
+    // second issuing thread lets these MMAs interleave on the tensor core with
+    // issuer A's S^T / dP^T of the next tile (one issuer alone is limited by
+    // per-instruction issue cost, not by the tensor core).  Its commits only
+    // track its own MMAs; those of issuer A for tile i are complete before the
+    // softmax warps signal DSREADY(i).
+    if (lane == 0) {
+      constexpr uint32_t swz = swizzle_field(C::SWB);
+      constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
+      constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
+                                        : make_idesc_f16(C::BM, D, true, true);  // dQ
+      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
       for (int i = 0; ok && i < nq; ++i) {
         const int st = i % C::NST;
-        // Next tile's S^T / dP^T as soon as the softmax warps hold this tile's in registers.
-        if (i + 1 < nq) {
-          const int st1 = (i + 1) % C::NST;
-          if (!mbar_wait(bar(C_QFULL + st1), (uint32_t)((i + 1) / C::NST) & 1u, wc) ||
-              !mbar_wait(bar(C_SFREE), (uint32_t)i & 1u, wc))
-            break;
-          tc_fence_after();
-          issue_s_dp(i + 1);
-        }
         if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
+        TRACE(4, i);
         tc_fence_after();
         const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
-        // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
+        // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM); A from TMEM
 #pragma unroll
         for (int kk = 0; kk < C::BM / 16; ++kk) {
-          const int a = kk / 4;
-          const uint32_t koff = (uint32_t)(kk % 4) * 32u;
-          const uint64_t pd = make_smem_desc(sbase + C::OFF_P + a * C::BN * 128 + koff, 16, 1024, 2);
           const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-          mma_f16_ss(tmem + C::COL_DV, pd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < C::BM / 16; ++kk) {
-          const int a = kk / 4;
-          const uint32_t koff = (uint32_t)(kk % 4) * 32u;
-          const uint64_t sd =
-              make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
           const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-          mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (C::DS_TMEM) {
+            mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
+                       (i > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const int a = kk / 4;
+            const uint32_t koff = (uint32_t)(kk % 4) * 32u;
+            const uint64_t sd =
+                make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
+            mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         if (i > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(i - 1) & 1u, wc)) break;
+        TRACE(5, i);
         tc_fence_after();
         // dQ partial over this key tile (K = 128 key rows)
 #pragma unroll
@@ -312,6 +349,7 @@ __global__ void __launch_bounds__(448, 1)
         mma_commit(bar(C_DQFULL));
         mma_commit(bar(C_QEMPTY + st));
         mma_commit(bar(C_PFREE));
+        TRACE(6, i);
       }
       mma_commit(bar(C_KVDONE));
     }
@@ -333,6 +371,7 @@ __global__ void __launch_bounds__(448, 1)
         ok = false;
         break;
       }
+      if (threadIdx.x == 0) TRACE(7, i);
       tc_fence_after();
       uint32_t sr[HW], dr[HW];
 #pragma unroll
@@ -346,44 +385,59 @@ __global__ void __launch_bounds__(448, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C_SFREE));
+      if (threadIdx.x == 0) TRACE(8, i);
       const float* lse_s = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * C::BM * 4);
       const float* del_s = reinterpret_cast<const float*>(smem + C::OFF_DELTA + st * C::BM * 4);
-      // P^T and dS^T for this thread's HW query columns, packed to fp16 pairs in place
+      // P^T and dS^T for this thread's HW query columns, packed to fp16 pairs
       uint32_t pp[HW / 2], dd[HW / 2];
 #pragma unroll
-      for (int e = 0; e < HW; e += 2) {
-        float p2[2], d2[2];
+      for (int e = 0; e < HW; e += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + c0 + e);
+        const float4 d4 = *reinterpret_cast<const float4*>(del_s + c0 + e);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        const float dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float p4[4], ds4[4];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int ql = c0 + e + u;
           const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
-          const float pe =
-              valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lse_s[ql])) : 0.f;
-          p2[u] = pe;
-          d2[u] = pe * (__uint_as_float(dr[e + u]) - del_s[ql]);
+          const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lv[u])) : 0.f;
+          p4[u] = pe;
+          ds4[u] = pe * (__uint_as_float(dr[e + u]) - dv4[u]);
         }
-        pp[e / 2] = pack_half2(p2[0], p2[1]);
-        dd[e / 2] = pack_half2(d2[0], d2[1]);
+        pp[e / 2] = pack_half2(p4[0], p4[1]);
+        pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
+        dd[e / 2] = pack_half2(ds4[0], ds4[1]);
+        dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
       }
+      if (threadIdx.x == 0) TRACE(11, i);
       if (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc)) {
         ok = false;
         break;
       }
-      // Write to the [key row][query col] K-major SW128 tiles (64-column atoms)
+      if (threadIdx.x == 0) TRACE(9, i);
+      // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
+      // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
+      if constexpr (HW == 32) {
+        tmem_st16(tmem + lane_base + C::COL_PT + c0 / 2, pp);
+        if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + c0 / 2, dd);
+      } else {
+        tmem_st32(tmem + lane_base + C::COL_PT + c0 / 2, pp);
+        if constexpr (C::DS_TMEM) tmem_st32(tmem + lane_base + C::COL_DST + c0 / 2, dd);
+      }
       const int a = c0 / 64;
       const int ch0 = (c0 % 64) / 8;
-      const uint32_t pb = sbase + C::OFF_P + a * C::BN * 128;
       const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
 #pragma unroll
-      for (int u = 0; u < HW / 8; ++u) {
-        st_shared_v4(pb + sw128_offset(r, ch0 + u), pp[4 * u], pp[4 * u + 1], pp[4 * u + 2],
-                     pp[4 * u + 3]);
+      for (int u = 0; u < HW / 8; ++u)
         st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
                      dd[4 * u + 3]);
-      }
+      tmem_wait_st();
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C_DSREADY));
+      if (threadIdx.x == 0) TRACE(10, i);
     }
     // ------------------------------------------------------------ dK / dV epilogue
     constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
@@ -429,6 +483,7 @@ __global__ void __launch_bounds__(448, 1)
       const int sbuf = i % C::NDQ;
       const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
       if (!mbar_wait(bar(C_DQFULL), (uint32_t)i & 1u, wc)) break;
+      if (tid == 0) TRACE(12, i);
       tc_fence_after();
       if constexpr (C::DQT) {
         // TMEM lane = d, column = query row
@@ -440,6 +495,16 @@ __global__ void __launch_bounds__(448, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_DQFREE));
+#if defined(FA_BWD_EXPERIMENT) && FA_BWD_EXPERIMENT == 3
+        {
+          float* base = dq_acc + ((size_t)bh * S_pad + q0) * D + d;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) red_add_f32(base + (size_t)e * D, __uint_as_float(v0[e]));
+#pragma unroll
+          for (int e = 0; e < 32; ++e) red_add_f32(base + (size_t)(32 + e) * D, __uint_as_float(v1[e]));
+          continue;
+        }
+#endif
         if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
         named_bar_sync(1, 128);
 #if defined(FA_BWD_EXPERIMENT) && FA_BWD_EXPERIMENT == 2
@@ -484,6 +549,7 @@ __global__ void __launch_bounds__(448, 1)
         bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
 #endif
         bulk_commit_group();
+        TRACE(13, i);
       }
     }
     if (tid == 0) bulk_wait_group_all();
@@ -543,3 +609,9 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
 }
 
 }  // namespace fa_sm100
+
+#ifdef FA_BWD_TRACE
+extern "C" int fa_debug_trace(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_trace, sizeof(fa_sm100::g_trace));
+}
+#endif

@@ -25,10 +25,10 @@
 //                stage it in shared memory and add it into the fp32 accumulator
 //                with one bulk reduction (cp.reduce.async.bulk .add.f32).
 //     warp 12    TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
-//     warp 13    MMA issuer A: S^T = K Q^T, dP^T = V dO^T of each tile, issued
-//                as soon as the previous tile's S^T / dP^T are in registers.
-//     warp 14    MMA issuer B: dV += P^T dO, dK += dS^T Q, dQ partial = dS K
-//                (stored transposed for D=128).
+//     warps 13-16 MMA issuers, one per independent chain: S^T = K Q^T,
+//                dP^T = V dO^T (issued as soon as the previous tile's values are
+//                in registers), dV += P^T dO with dK += dS^T Q, and the dQ
+//                partial = dS K (stored transposed for D=128).
 //   fa_bwd_post  dQ = fp16(scale * accumulator) in (B, S, H, D).
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,6 +40,8 @@
 namespace fa_sm100 {
 
 #ifdef FA_BWD_TRACE
+// Debug build only: clock64() stamps of barrier events of CTA (0, 0), read
+// back with fa_debug_trace().
 __device__ unsigned long long g_trace[64][16];
 #define TRACE(slot, it)                                                              \
   do {                                                                               \
@@ -77,7 +79,7 @@ struct BwdCfg {
   static constexpr int OFF_DQS = OFF_DS + PT_BYTES;
   static constexpr int SMEM = OFF_DQS + NDQ * DQ_STAGE_BYTES + 1024;  // + alignment slack
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 480;
+  static constexpr int THREADS = 544;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
   static constexpr uint32_t COL_DV = DQT ? 256 : 384;
@@ -165,7 +167,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __r
 
 // -------------------------------------------------------------------------- main
 template <int D>
-__global__ void __launch_bounds__(480, 1)
+__global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(480, 1)
     for (int i = 0; i < C_COUNT; ++i) {
       uint32_t cnt = 1;
       if (i == C_SFREE || i == C_DSREADY) cnt = 8;
+      if (i == C_SFULL || i == C_PFREE) cnt = 2;  // two issuing threads commit
       if (i == C_DQFREE) cnt = 4;
       mbar_init(bar(i), cnt);
     }
@@ -247,111 +250,101 @@ __global__ void __launch_bounds__(480, 1)
                   C::BM * 4, bar(C_QFULL + st));
       }
     }
-  } else if (warp == 13) {
-    // ------------------------------------------------------------ MMA issuer A
+  } else if (warp >= 13) {
+    // ------------------------------------------------------------ MMA issuers (warps 13..16)
+    // Each independent MMA chain has its own issuing thread: one thread can have
+    // only about one tcgen05.mma in setup at a time (~90 clk each), so a single
+    // issuer leaves the tensor core idle on these small tiles, while four
+    // concurrent issuers keep it busy.  Roles:
+    //   0: S^T = K Q^T        1: dP^T = V dO^T      (tile i, once the softmax
+    //                                                warps hold tile i-1's values)
+    //   2: dV += P^T dO, dK += dS^T Q (A operands in TMEM)
+    //   3: dQ partial = dS K (transposed for D=128)
+    // A commit only tracks its own thread's MMAs; barriers that need several
+    // chains expect one arrival per chain (SFULL: 0+1, PFREE: 2+3).  Tile i's
+    // S^T / dP^T are complete before the softmax warps signal DSREADY(i).
+    const int role = warp - 13;
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
       constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false);   // S^T, dP^T
-      // S^T = K Q^T and dP^T = V dO^T for query tile i (M = 128 key rows, N = BM, K = D)
-      auto issue_s_dp = [&](int i) {
-        const int st = i % C::NST;
-        const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
-        const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int a = (kk * 16) / C::AE;
-          const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
-          const uint64_t ad = make_smem_desc(sbase + C::OFF_K + a * C::BN * C::SWB + koff, 16,
-                                             8 * C::SWB, swz);
-          const uint64_t bd = make_smem_desc(qb + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
-          mma_f16_ss(tmem + C::COL_S, ad, bd, id_s, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int a = (kk * 16) / C::AE;
-          const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
-          const uint64_t ad = make_smem_desc(sbase + C::OFF_V + a * C::BN * C::SWB + koff, 16,
-                                             8 * C::SWB, swz);
-          const uint64_t bd = make_smem_desc(dob + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
-          mma_f16_ss(tmem + C::COL_DP, ad, bd, id_s, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(C_SFULL));
-      };
-      // Issuer A (warp 13): S^T / dP^T of every query tile, each as soon as the
-      // softmax warps hold the previous tile's values in registers.
-      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
-      for (int i = 0; ok && i < nq; ++i) {
-        if (!mbar_wait(bar(C_QFULL + i % C::NST), (uint32_t)(i / C::NST) & 1u, wc) ||
-            (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)))
-          break;
-        TRACE(2, i);
-        tc_fence_after();
-        issue_s_dp(i);
-        TRACE(3, i);
-      }
-    }
-  } else if (warp == 14) {
-    // ------------------------------------------------------------ MMA issuer B
-    // dV, dK and the dQ partial of each tile once its P^T / dS^T are ready.  A
-    // second issuing thread lets these MMAs interleave on the tensor core with
-    // issuer A's S^T / dP^T of the next tile (one issuer alone is limited by
-    // per-instruction issue cost, not by the tensor core).  Its commits only
-    // track its own MMAs; those of issuer A for tile i are complete before the
-    // softmax warps signal DSREADY(i).
-    if (lane == 0) {
-      constexpr uint32_t swz = swizzle_field(C::SWB);
       constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
       constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
                                         : make_idesc_f16(C::BM, D, true, true);  // dQ
       bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
       for (int i = 0; ok && i < nq; ++i) {
         const int st = i % C::NST;
-        if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
-        TRACE(4, i);
-        tc_fence_after();
         const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
-        // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM); A from TMEM
+        if (role <= 1) {
+          // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
+          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc) ||
+              (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)))
+            break;
+          if (role == 0) TRACE(2, i);
+          tc_fence_after();
+          const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
+          const uint32_t bbase = role == 0 ? qb : dob;
+          const uint32_t dcol = tmem + (role == 0 ? C::COL_S : C::COL_DP);
 #pragma unroll
-        for (int kk = 0; kk < C::BM / 16; ++kk) {
-          const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-          mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < C::BM / 16; ++kk) {
-          const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-          if constexpr (C::DS_TMEM) {
-            mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
-                       (i > 0 || kk > 0) ? 1u : 0u);
-          } else {
-            const int a = kk / 4;
-            const uint32_t koff = (uint32_t)(kk % 4) * 32u;
-            const uint64_t sd =
-                make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
-            mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int a = (kk * 16) / C::AE;
+            const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
+            const uint64_t ad = make_smem_desc(abase + a * C::BN * C::SWB + koff, 16, 8 * C::SWB, swz);
+            const uint64_t bd = make_smem_desc(bbase + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
+            mma_f16_ss(dcol, ad, bd, id_s, kk > 0 ? 1u : 0u);
           }
-        }
-        if (i > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(i - 1) & 1u, wc)) break;
-        TRACE(5, i);
-        tc_fence_after();
-        // dQ partial over this key tile (K = 128 key rows)
+          mma_commit(bar(C_SFULL));
+          if (role == 0) TRACE(3, i);
+        } else if (role == 2) {
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
+          TRACE(4, i);
+          tc_fence_after();
+          // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
 #pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t dsd =
-              make_smem_desc(sbase + C::OFF_DS + kk * 16 * 128, C::BN * 128, 1024, 2);
-          const uint64_t kd =
-              make_smem_desc(sbase + C::OFF_K + kk * 16 * C::SWB, C::BN * C::SWB, 8 * C::SWB, swz);
-          if constexpr (C::DQT)
-            mma_f16_ss(tmem + C::COL_DQ, kd, dsd, id_dq, kk > 0 ? 1u : 0u);  // K^T dS^T
-          else
-            mma_f16_ss(tmem + C::COL_DQ, dsd, kd, id_dq, kk > 0 ? 1u : 0u);  // dS K
+          for (int kk = 0; kk < C::BM / 16; ++kk) {
+            const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+            mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::BM / 16; ++kk) {
+            const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+            if constexpr (C::DS_TMEM) {
+              mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
+                         (i > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const int a = kk / 4;
+              const uint32_t koff = (uint32_t)(kk % 4) * 32u;
+              const uint64_t sd =
+                  make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
+              mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(bar(C_QEMPTY + st));
+          mma_commit(bar(C_PFREE));
+          TRACE(6, i);
+        } else {
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc) ||
+              (i > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(i - 1) & 1u, wc)))
+            break;
+          TRACE(5, i);
+          tc_fence_after();
+          // dQ partial over this key tile (K = 128 key rows)
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {
+            const uint64_t dsd =
+                make_smem_desc(sbase + C::OFF_DS + kk * 16 * 128, C::BN * 128, 1024, 2);
+            const uint64_t kd =
+                make_smem_desc(sbase + C::OFF_K + kk * 16 * C::SWB, C::BN * C::SWB, 8 * C::SWB, swz);
+            if constexpr (C::DQT)
+              mma_f16_ss(tmem + C::COL_DQ, kd, dsd, id_dq, kk > 0 ? 1u : 0u);  // K^T dS^T
+            else
+              mma_f16_ss(tmem + C::COL_DQ, dsd, kd, id_dq, kk > 0 ? 1u : 0u);  // dS K
+          }
+          mma_commit(bar(C_DQFULL));
+          mma_commit(bar(C_PFREE));
         }
-        mma_commit(bar(C_DQFULL));
-        mma_commit(bar(C_QEMPTY + st));
-        mma_commit(bar(C_PFREE));
-        TRACE(6, i);
       }
-      mma_commit(bar(C_KVDONE));
+      if (role == 2) mma_commit(bar(C_KVDONE));
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax / dS warps 0..7
@@ -495,21 +488,8 @@ __global__ void __launch_bounds__(480, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_DQFREE));
-#if defined(FA_BWD_EXPERIMENT) && FA_BWD_EXPERIMENT == 3
-        {
-          float* base = dq_acc + ((size_t)bh * S_pad + q0) * D + d;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) red_add_f32(base + (size_t)e * D, __uint_as_float(v0[e]));
-#pragma unroll
-          for (int e = 0; e < 32; ++e) red_add_f32(base + (size_t)(32 + e) * D, __uint_as_float(v1[e]));
-          continue;
-        }
-#endif
         if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
         named_bar_sync(1, 128);
-#if defined(FA_BWD_EXPERIMENT) && FA_BWD_EXPERIMENT == 2
-        if (d < 0)
-#endif
 #pragma unroll
         for (int e = 0; e < 32; ++e) st_shared_f32(stage + (uint32_t)(e * D + d) * 4u, __uint_as_float(v0[e]));
 #pragma unroll
@@ -545,9 +525,7 @@ __global__ void __launch_bounds__(480, 1)
       fence_proxy_async_smem();
       named_bar_sync(1, 128);
       if (tid == 0) {
-#if !defined(FA_BWD_EXPERIMENT) || FA_BWD_EXPERIMENT == 0
         bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
-#endif
         bulk_commit_group();
         TRACE(13, i);
       }

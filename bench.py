@@ -50,6 +50,12 @@ WORKLOADS = {
 }
 
 
+# DRAM bytes (read + write) per launch of the main backward kernel, from one ncu
+# capture of a 1/16-size case scaled by the (batch, head) count; see
+# profiles/fa_kernels_d128_s8192_full.md.
+BWD_TRAFFIC_PER_LAUNCH = {"c4": 4.71e9}
+
+
 def flops_fwd(B, S, H, D, causal):
     f = 4.0 * B * H * S * S * D
     return f * 0.5 if causal else f
@@ -98,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu_index)],
+                 "-lms", "50", "-i", str(self.gpu_index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -343,7 +349,8 @@ def run_ours(args, wl):
                     "d2h_bytes_per_step": 4 * nb, "steps": e2e_steps},
             "roofline": {"bound": "tensor", "kernel": f"fa_bwd_main_kernel<{D}>",
                          "achieved": k_tflops, "peak": peak_burst, "unit": "TFLOP/s",
-                         "frac": k_tflops / peak_burst, "traffic": None,
+                         "frac": k_tflops / peak_burst,
+                         "traffic": BWD_TRAFFIC_PER_LAUNCH.get(wl) if world == 1 else None,
                          "peak_kind": f"{peak_kind} bf16 burst",
                          "flops_per_launch": bwd_alg, "mean_ms": k_ms,
                          "fwd_kernel": {"achieved": f_tflops, "mean_ms": f_ms,

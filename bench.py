@@ -393,18 +393,130 @@ def bench_small(wl, dev, args):
             "tflops": f / (ms * 1e-3) / 1e12, "l2": "flushed (256 MiB write) before each step"}
 
 
+# ----------------------------------------------------------------------- config 5
+C5 = dict(layers=24, hidden=2048, heads=16, head_dim=128, mlp=5504, vocab=32000, batch=8,
+          seq=2048)
+
+
+class _EventMark(torch.autograd.Function):
+    """Identity whose backward records a CUDA event (brackets a backward region)."""
+
+    @staticmethod
+    def forward(ctx, x, sink):
+        ctx.sink = sink
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        ctx.sink.append(e)
+        return g, None
+
+
+def run_c5(args):
+    """Config 5: random-init LLaMA-style decoder patched with patch_hf; one step =
+    forward + shifted-label cross-entropy + backward + SGD update on 8 x 2048
+    uniform token ids.  `value` is the attention fwd+bwd TFLOP/s measured inside
+    the step (CUDA events around every attention call and its backward)."""
+    import transformers as T
+    from flash_attn_volta_b200 import patch_hf
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = C5
+    cfg = T.LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"],
+                        intermediate_size=c["mlp"], num_hidden_layers=c["layers"],
+                        num_attention_heads=c["heads"], num_key_value_heads=c["heads"],
+                        head_dim=c["head_dim"], rope_theta=10000.0, initializer_range=0.02,
+                        max_position_embeddings=c["seq"])
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = T.LlamaForCausalLM(cfg).to(torch.float16)
+    fam, n = patch_hf.patch_model(model)
+    assert fam == "llama" and n == c["layers"]
+    fwd_ev, bwd_ev = [], []
+    base = patch_hf.flash_attn
+
+    def timed_attn(q, k, v, causal=False, sm_scale=None):
+        q = _EventMark.apply(q, bwd_ev)      # backward of this runs after attention's backward
+        e0 = torch.cuda.Event(enable_timing=True); e0.record()
+        out = base(q, k, v, causal=causal, sm_scale=sm_scale)
+        e1 = torch.cuda.Event(enable_timing=True); e1.record()
+        fwd_ev.append((e0, e1))
+        return _EventMark.apply(out, bwd_ev)  # backward of this runs just before it
+
+    patch_hf.flash_attn = timed_attn
+    g = torch.Generator().manual_seed(1)
+    host_ids = torch.randint(0, c["vocab"], (c["batch"], c["seq"]), generator=g).pin_memory()
+    params = [p for p in model.parameters()]
+    lr = 1e-4
+
+    def step():
+        ids = host_ids.to(dev, non_blocking=True)
+        for p in params:
+            p.grad = None
+        loss = model(ids, labels=ids).loss
+        loss.backward()
+        with torch.no_grad():
+            torch._foreach_add_(params, [p.grad for p in params], alpha=-lr)
+        return loss
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    fwd_ev.clear(); bwd_ev.clear()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    losses = [step() for _ in range(args.steps)]
+    t1.record()
+    torch.cuda.synchronize(dev)
+    clock_info = clocks.stop()
+    step_ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = sum(a.elapsed_time(b) for a, b in fwd_ev)
+    # bwd events come in pairs per layer: (before attention bwd, after attention bwd)
+    attn_ms += sum(bwd_ev[i].elapsed_time(bwd_ev[i + 1]) for i in range(0, len(bwd_ev), 2))
+    attn_ms /= args.steps
+    f_layer = 2.5 * flops_fwd(c["batch"], c["seq"], c["heads"], c["head_dim"], True)
+    value = c["layers"] * f_layer / (attn_ms * 1e-3) / 1e12
+    peak_burst, peak_sus, peak_kind = load_peaks()
+    line = {
+        "metric": "attention fwd+bwd TFLOP/s", "value": value, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (uniform token ids, random-init N(0,0.02) weights)",
+        "config": {"workload": "c5", **c, "attention_ms_per_step": attn_ms,
+                   "attention_share_of_step": attn_ms / step_ms,
+                   "tokens_per_s": c["batch"] * c["seq"] / (step_ms * 1e-3),
+                   "loss_first_last": [losses[0].item(), losses[-1].item()],
+                   "flop_convention": "per layer 2.5 x 4*B*H*S^2*D / 2 (causal)"},
+        "pct_of_peak": {"value": value / peak_sus, "peak_tflops": peak_sus,
+                        "kind": f"{peak_kind} bf16 sustained"},
+        "gpu_launches": 4 * c["layers"] * args.steps,
+        "e2e": {"value": value, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": 0},
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5"], default="c4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args, args.workload)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_ours(args, args.workload)
 

@@ -503,13 +503,66 @@ def run_c5(args):
     print(json.dumps(line), flush=True)
 
 
+def run_ring(args):
+    """Config 5, long variant: B=1, S=131072, H=32, D=128, causal; ring context
+    parallelism over the N ranks (zigzag shards, NCCL send/recv of K/V blocks).
+    Strong scaling: the whole sequence is fixed and split across ranks."""
+    import torch.distributed as dist
+    from flash_attn_volta_b200 import ring
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    B, S, H, D, causal = 1, 131072, 32, 128, True
+    g = torch.Generator(device=dev).manual_seed(7)
+    full = lambda: torch.randn((B, S, H, D), device=dev, generator=g, dtype=torch.float16)
+    q, k, v, do = (ring.zigzag_shard(full(), rank, world) for _ in range(4))
+    for t in (q, k, v):
+        t.requires_grad_()
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        ring.ring_flash_attn(q, k, v, causal=causal).backward(do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = time_steps(step, args.steps, torch.cuda.current_stream(dev))
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total = 2.5 * flops_fwd(B, S, H, D, causal) * args.steps
+    value = total / (ms * 1e-3) / 1e12
+    peak_burst, peak_sus, peak_kind = load_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "attention fwd+bwd TFLOP/s", "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "c5long", "B": B, "S": S, "H": H, "D": D, "causal": causal,
+                       "parallelism": f"ring-cp{world} (zigzag)",
+                       "l2": "inputs (1 GiB per tensor) larger than L2"},
+            "pct_of_peak": {"value": value / (world * peak_sus), "peak_tflops": world * peak_sus,
+                            "kind": f"{peak_kind} bf16 sustained x n_gpus"},
+            "gpu_launches": None,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5"], default="c4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5", "c5long"], default="c4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
@@ -517,6 +570,8 @@ def main():
         run_reference(args, args.workload)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload == "c5long":
+        run_ring(args)
     else:
         run_ours(args, args.workload)
 

@@ -1,0 +1,213 @@
+"""Ring context-parallel attention over the sequence axis (NCCL send/recv).
+
+For sequences too long for one GPU's time budget (long
+variant: B=1, S=131072, H=32, D=128, causal over 8 GPUs).  The reference has
+no multi-GPU path; this is the build's own design on top of the single-GPU
+kernels:
+
+* Zigzag sharding: the sequence is cut into 2·G chunks of C = S / (2G) rows
+  and rank r holds chunks r and 2G-1-r of q, k, v (and o, dO).  Under a causal
+  mask every rank then has the same amount of work.
+* Forward: G steps; at step s rank r holds the K/V chunks of rank (r - s) mod G
+  and computes its two query chunks against them.  A (query chunk i, key chunk
+  j) block is skipped if j > i, causal if j == i and full if j < i (without a
+  causal mask every block is full).  Every block is a square C x C attention —
+  exactly what the single-GPU kernel computes — returning (O_ij, LSE_ij); the
+  partial results are merged with lse = logaddexp(lse, lse_ij) and
+  O = sum_j exp(lse_ij - lse) O_ij in fp32.  The next K/V block is exchanged
+  (batch_isend_irecv to r+1 / from r-1) while the current one is computed.
+* Backward: the same ring; each block's (dq, dk, dv) come from the single-GPU
+  backward fed with the *final* O and LSE (so P and delta are the global ones,
+  as in the reference's Algorithm-4 backward); dq accumulates locally and
+  dk/dv accumulate in an fp32 buffer that travels with its K/V block and makes
+  one last hop back to its owner.
+
+Received blocks land in local buffers before a kernel reads them: no kernel
+touches another GPU's memory.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .backward import flash_attn_backward
+from .forward import flash_attn_forward
+
+
+def _kernel_block_fwd(q, k, v, causal, scale):
+    return flash_attn_forward(q, k, v, causal=causal, sm_scale=scale, return_softmax_lse=True)
+
+
+def _kernel_block_bwd(do, q, k, v, o, lse, causal, scale):
+    return flash_attn_backward(do, q, k, v, o, lse, causal=causal, sm_scale=scale)
+
+
+# The per-block computations; the CPU tests substitute the oracle here.
+block_fwd = _kernel_block_fwd
+block_bwd = _kernel_block_bwd
+
+
+def zigzag_chunk_ids(rank: int, world: int) -> tuple[int, int]:
+    return rank, 2 * world - 1 - rank
+
+
+def zigzag_shard(x: torch.Tensor, rank: int, world: int, dim: int = 1) -> torch.Tensor:
+    """This rank's two chunks of x along `dim`, concatenated (length 2*S/(2*world))."""
+    S = x.shape[dim]
+    assert S % (2 * world) == 0, f"sequence length {S} not divisible by 2*world={2 * world}"
+    chunks = x.chunk(2 * world, dim=dim)
+    a, b = zigzag_chunk_ids(rank, world)
+    return torch.cat([chunks[a], chunks[b]], dim=dim).contiguous()
+
+
+def zigzag_unshard(shards: list, dim: int = 1) -> torch.Tensor:
+    """Inverse of zigzag_shard given every rank's shard (rank order)."""
+    world = len(shards)
+    chunks = [None] * (2 * world)
+    for r, s in enumerate(shards):
+        a, b = zigzag_chunk_ids(r, world)
+        chunks[a], chunks[b] = s.chunk(2, dim=dim)
+    return torch.cat(chunks, dim=dim)
+
+
+def _block_mode(i: int, j: int, causal: bool):
+    """None = skip, True = causal (diagonal) block, False = full block."""
+    if not causal:
+        return False
+    if j > i:
+        return None
+    return j == i
+
+
+def _merge(acc_o, acc_lse, o, lse):
+    """Merge a block's (o (B,C,H,D), lse (B,H,C)) into the fp32 running result."""
+    o = o.float()
+    if acc_o is None:
+        return o, lse.clone()
+    new = torch.logaddexp(acc_lse, lse)
+    w_old = torch.exp(acc_lse - new).transpose(1, 2).unsqueeze(-1)
+    w_new = torch.exp(lse - new).transpose(1, 2).unsqueeze(-1)
+    return acc_o * w_old + o * w_new, new
+
+
+def _exchange(send: torch.Tensor, group, rank: int, world: int):
+    """Start sending `send` to rank+1 and receiving the same shape from rank-1."""
+    recv = torch.empty_like(send)
+    nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
+    prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
+    ops = [dist.P2POp(dist.isend, send, nxt, group), dist.P2POp(dist.irecv, recv, prv, group)]
+    reqs = dist.batch_isend_irecv(ops)
+    return recv, reqs
+
+
+def _world(group):
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _ring_forward(q2, k2, v2, causal, scale, group):
+    rank, world = _world(group)
+    q = q2.chunk(2, dim=1)
+    ids_q = zigzag_chunk_ids(rank, world)
+    kv = torch.stack([k2, v2])  # (2, B, 2C, H, D): travels as one buffer
+    acc = [[None, None], [None, None]]  # per query chunk: [o, lse]
+    for step in range(world):
+        src = (rank - step) % world
+        ids_k = zigzag_chunk_ids(src, world)
+        pending = _exchange(kv, group, rank, world) if step < world - 1 else None
+        ks, vs = kv[0].chunk(2, dim=1), kv[1].chunk(2, dim=1)
+        for a in range(2):
+            for b in range(2):
+                mode = _block_mode(ids_q[a], ids_k[b], causal)
+                if mode is None:
+                    continue
+                o, lse = block_fwd(q[a].contiguous(), ks[b].contiguous(), vs[b].contiguous(),
+                                   mode, scale)
+                acc[a] = list(_merge(acc[a][0], acc[a][1], o, lse))
+        if pending is not None:
+            recv, reqs = pending
+            for r in reqs:
+                r.wait()
+            kv = recv
+    o = torch.cat([acc[0][0], acc[1][0]], dim=1).to(q2.dtype)
+    lse = torch.cat([acc[0][1], acc[1][1]], dim=2).contiguous()
+    return o, lse
+
+
+def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
+    rank, world = _world(group)
+    q, do, o = q2.chunk(2, dim=1), do2.chunk(2, dim=1), o2.chunk(2, dim=1)
+    lse = lse2.chunk(2, dim=2)
+    ids_q = zigzag_chunk_ids(rank, world)
+    dq = torch.zeros(q2.shape, dtype=torch.float32, device=q2.device)
+    dqs = dq.chunk(2, dim=1)
+    kv = torch.stack([k2, v2])
+    dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q2.device)
+    for step in range(world):
+        src = (rank - step) % world
+        ids_k = zigzag_chunk_ids(src, world)
+        pending = _exchange(kv, group, rank, world) if step < world - 1 else None
+        ks, vs = kv[0].chunk(2, dim=1), kv[1].chunk(2, dim=1)
+        dks, dvs = dkv[0].chunk(2, dim=1), dkv[1].chunk(2, dim=1)
+        for a in range(2):
+            for b in range(2):
+                mode = _block_mode(ids_q[a], ids_k[b], causal)
+                if mode is None:
+                    continue
+                g = block_bwd(do[a].contiguous(), q[a].contiguous(), ks[b].contiguous(),
+                              vs[b].contiguous(), o[a].contiguous(), lse[a].contiguous(), mode,
+                              scale)
+                dqs[a].add_(g[0].float())
+                dks[b].add_(g[1].float())
+                dvs[b].add_(g[2].float())
+        # the dK/dV accumulator follows its K/V block; after the last step it
+        # makes one more hop, which brings every block's gradients home
+        if world > 1:
+            recv_dkv, reqs = _exchange(dkv, group, rank, world)
+            for r in reqs:
+                r.wait()
+            dkv = recv_dkv
+        if pending is not None:
+            recv, reqs = pending
+            for r in reqs:
+                r.wait()
+            kv = recv
+    return dq.to(q2.dtype), dkv[0].to(k2.dtype), dkv[1].to(v2.dtype)
+
+
+class _RingFlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, sm_scale, group):
+        o, lse = _ring_forward(q, k, v, causal, sm_scale, group)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal, ctx.sm_scale, ctx.group = causal, sm_scale, group
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = do.contiguous().to(q.dtype)
+        dq, dk, dv = _ring_backward(do, q, k, v, o, lse, ctx.causal, ctx.sm_scale, ctx.group)
+        return dq, dk, dv, None, None, None
+
+
+def ring_flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                    sm_scale: Optional[float] = None, group=None) -> torch.Tensor:
+    """Attention over a sequence sharded across the ranks of `group` (zigzag).
+
+    Args:
+        q, k, v: this rank's zigzag shard, (B, 2*C, H, D) — see zigzag_shard.
+        causal: top-left causal mask over the full (unsharded) sequence.
+        sm_scale: softmax scale (default 1/sqrt(D)).
+        group: process group (default: the world).
+
+    Returns the rank's shard of the output, same layout; autograd-aware.
+    """
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    assert q.shape == k.shape == v.shape and q.shape[1] % 2 == 0
+    return _RingFlashAttnFn.apply(q, k, v, causal, sm_scale, group)

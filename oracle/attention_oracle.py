@@ -38,6 +38,7 @@ __all__ = [
     "attention_bwd",
     "attention_fwd_tiled",
     "attention_rows",
+    "attention_bwd_given_lse",
     "flops_fwd",
     "flops_fwdbwd",
 ]
@@ -93,6 +94,36 @@ def attention_bwd(do, q, k, v, causal=False, scale=None, dtype=torch.float64):
     delta = (oh * doh).sum(-1, keepdim=True)                 # triton_fa_bwd.py:650
     dv = torch.einsum("bhnm,bhnd->bhmd", p, doh)              # P^T dO
     dp = torch.einsum("bhnd,bhmd->bhnm", doh, vh)             # dO V^T
+    ds = p * (dp - delta)
+    dq = torch.einsum("bhnm,bhmd->bhnd", ds, kh) * scale
+    dk = torch.einsum("bhnm,bhnd->bhmd", ds, qh) * scale
+    back = lambda t: t.permute(0, 2, 1, 3).contiguous()
+    return back(dq), back(dk), back(dv)
+
+
+def attention_bwd_given_lse(do, q, k, v, o, lse, causal=False, scale=None,
+                            dtype=torch.float64):
+    """Backward of one (query block, key block) pair given the *global* output O
+    and log-sum-exp: P = exp(S - LSE) (triton_fa_bwd.py:165), delta =
+    rowsum(O*dO) (:650), dS = P (dP - delta) (:172), dQ = scale dS K,
+    dK = scale dS^T Q, dV = P^T dO.  With O and LSE of the block alone this is
+    the ordinary backward; with those of a longer key range it is that block's
+    share of the gradients.  Returns (dq, dk, dv) like `attention_bwd`.
+    """
+    D = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    s = _scores(q, k, causal, scale, dtype)
+    p = torch.exp(s - lse.to(dtype)[..., None])
+    p = torch.nan_to_num(p, nan=0.0)
+    vh = v.permute(0, 2, 1, 3).to(dtype)
+    qh = q.permute(0, 2, 1, 3).to(dtype)
+    kh = k.permute(0, 2, 1, 3).to(dtype)
+    doh = do.permute(0, 2, 1, 3).to(dtype)
+    oh = o.permute(0, 2, 1, 3).to(dtype)
+    delta = (oh * doh).sum(-1, keepdim=True)
+    dv = torch.einsum("bhnm,bhnd->bhmd", p, doh)
+    dp = torch.einsum("bhnd,bhmd->bhnm", doh, vh)
     ds = p * (dp - delta)
     dq = torch.einsum("bhnm,bhmd->bhnd", ds, kh) * scale
     dk = torch.einsum("bhnm,bhnd->bhmd", ds, qh) * scale

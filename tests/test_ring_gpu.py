@@ -1,0 +1,85 @@
+"""Ring context-parallel attention with the real kernels.
+
+One GPU: a ring of one rank still splits the sequence into two zigzag chunks
+and merges three blocks (two causal, one full) — compared with the unsharded
+kernel and the oracle.  Two GPUs (when present): NCCL ranks as child
+processes, compared with the unsharded oracle.
+"""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from flash_attn_volta_b200 import flash_attn, ring
+from tests.helpers import TOL_GRAD, TOL_O, make_inputs, maxdiff, oracle_heads, pick_heads
+
+pytestmark = pytest.mark.gpu
+
+
+def test_ring_one_rank_matches_kernel_and_oracle():
+    dev = torch.device("cuda", 0)
+    B, S, H, D = 1, 2048, 4, 128
+    q, k, v, do = make_inputs(B, S, H, D, seed=11)
+    leaves = [t.to(dev).requires_grad_() for t in (q, k, v)]
+    o = ring.ring_flash_attn(*leaves, causal=True)
+    o.backward(do.to(dev))
+    heads = [(0, 0), (0, 3)]
+    ref = oracle_heads(q, k, v, do, True, 1 / math.sqrt(D), heads)
+    assert maxdiff(pick_heads(o.detach().cpu(), heads), ref["o"]) <= TOL_O
+    for g, n in zip(leaves, ("dq", "dk", "dv")):
+        assert maxdiff(pick_heads(g.grad.cpu(), heads), ref[n]) <= TOL_GRAD
+    full = flash_attn(*(t.to(dev) for t in (q, k, v)), causal=True)
+    assert maxdiff(o.detach(), full) <= TOL_O
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        dev = torch.device("cuda", rank)
+        q, k, v, do = make_inputs(1, 4096, 4, 128, seed=12)
+        sh = lambda t: ring.zigzag_shard(t, rank, world).to(dev)
+        qs, ks, vs = (sh(t).requires_grad_() for t in (q, k, v))
+        o = ring.ring_flash_attn(qs, ks, vs, causal=True)
+        o.backward(sh(do))
+        torch.cuda.synchronize(dev)
+        out_q.put((rank, o.detach().cpu(), qs.grad.cpu(), ks.grad.cpu(), vs.grad.cpu()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ring_two_gpus_matches_oracle():
+    world = 2
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, out_q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([out_q.get(timeout=300) for _ in range(world)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    o, dq, dk, dv = (ring.zigzag_unshard([r[i] for r in res]) for i in range(1, 5))
+    q, k, v, do = make_inputs(1, 4096, 4, 128, seed=12)
+    heads = [(0, 1), (0, 2)]
+    ref = oracle_heads(q, k, v, do, True, 1 / math.sqrt(128), heads)
+    assert maxdiff(pick_heads(o, heads), ref["o"]) <= TOL_O
+    for g, n in zip((dq, dk, dv), ("dq", "dk", "dv")):
+        assert maxdiff(pick_heads(g, heads), ref[n]) <= TOL_GRAD

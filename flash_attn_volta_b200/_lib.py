@@ -58,6 +58,8 @@ def load() -> ctypes.CDLL:
             lib.fa_sm100_bwd_workspace_bytes.restype = _c_size
             lib.fa_sm100_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
             lib.fa_sm100_set_wait_timeout_ns.restype = None
+            lib.fa_sm100_set_debug_flags.argtypes = [_c_int]
+            lib.fa_sm100_set_debug_flags.restype = None
             lib.fa_sm100_error_string.argtypes = [_c_int]
             lib.fa_sm100_error_string.restype = ctypes.c_char_p
             lib.fa_sm100_abi_version.argtypes = []

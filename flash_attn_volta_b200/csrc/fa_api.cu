@@ -22,6 +22,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 std::atomic<unsigned long long> g_timeout_ns{4000000000ull};
+std::atomic<int> g_debug_flags{0};
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
@@ -129,6 +130,8 @@ const char* fa_sm100_error_string(int code) {
 
 void fa_sm100_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 1ull); }
 
+void fa_sm100_set_debug_flags(int flags) { g_debug_flags.store(flags); }
+
 int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
                  int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
                  void* stream) {
@@ -156,6 +159,7 @@ int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* 
   a.causal = causal ? 1 : 0;
   a.status = status;
   a.timeout_ns = g_timeout_ns.load();
+  a.debug_flags = g_debug_flags.load();
   return launch_fwd(a, static_cast<cudaStream_t>(stream));
 }
 

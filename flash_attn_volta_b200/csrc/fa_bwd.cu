@@ -104,7 +104,8 @@ enum BwdBar {
   C_DQFULL = 12,
   C_DQFREE = 13,  // 4 arrivals
   C_KVDONE = 14,
-  C_COUNT = 15
+  C_DRAIN = 15,   // 4 arrivals: each MMA issuer's last commit
+  C_COUNT = 16
 };
 
 // -------------------------------------------------------------------------- pre
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(544, 1)
       uint32_t cnt = 1;
       if (i == C_SFREE || i == C_DSREADY) cnt = 8;
       if (i == C_SFULL || i == C_PFREE) cnt = 2;  // two issuing threads commit
-      if (i == C_DQFREE) cnt = 4;
+      if (i == C_DQFREE || i == C_DRAIN) cnt = 4;
       mbar_init(bar(i), cnt);
     }
     *abort_flag = 0;
@@ -230,6 +231,8 @@ __global__ void __launch_bounds__(544, 1)
         tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, h, b);
         tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, h, b);
       }
+      int q_last[C::NST];  // last query tile loaded into each stage
+      for (int t = 0; t < C::NST; ++t) q_last[t] = -1;
       for (int i = 0; i < nq; ++i) {
         const int st = i % C::NST;
         const uint32_t ph = (uint32_t)(i / C::NST) & 1u;
@@ -248,6 +251,14 @@ __global__ void __launch_bounds__(544, 1)
                   bar(C_QFULL + st));
         bulk_load(sbase + C::OFF_DELTA + st * C::BM * 4, delta + (size_t)bh * S_pad + q0,
                   C::BM * 4, bar(C_QFULL + st));
+        q_last[st] = i;
+      }
+      // After an abort, let the loads this CTA issued land before it exits.
+      if (*abort_flag) {
+        mbar_wait_drain(bar(C_KVFULL), 0, timeout_ns);
+        for (int t = 0; t < C::NST; ++t)
+          if (q_last[t] >= 0)
+            mbar_wait_drain(bar(C_QFULL + t), (uint32_t)(q_last[t] / C::NST) & 1u, timeout_ns);
       }
     }
   } else if (warp >= 13) {
@@ -345,6 +356,7 @@ __global__ void __launch_bounds__(544, 1)
         }
       }
       if (role == 2) mma_commit(bar(C_KVDONE));
+      mma_commit(bar(C_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax / dS warps 0..7
@@ -537,6 +549,8 @@ __global__ void __launch_bounds__(544, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 13) {
+    if (lane == 0) mbar_wait_drain(bar(C_DRAIN), 0, timeout_ns);
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

@@ -63,7 +63,8 @@ enum FwdBar {
   B_PFULL = 15,   // +2
   B_PFREE = 17,   // +2
   B_ODONE = 19,
-  B_COUNT = 20
+  B_DRAIN = 20,   // the MMA issuer's last commit: all its MMAs are complete
+  B_COUNT = 21
 };
 
 template <int D>
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(192, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
                   float* __restrict__ lse, int S, int H, float scale_log2, int causal, int* status,
-                  unsigned long long timeout_ns) {
+                  unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -120,6 +121,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive_expect_tx(bar(B_QFULL), C::Q_BYTES);
       for (int a = 0; a < C::NAT; ++a)
         tma_load_4d(sbase + C::OFF_Q + a * C::BM * C::SWB, &tm_q, bar(B_QFULL), a * C::AE, q0, h, b);
+      int k_last[C::NST], v_last[C::NST];  // last tile index loaded into each stage
+      for (int s = 0; s < C::NST; ++s) k_last[s] = v_last[s] = -1;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % C::NST;
         const uint32_t ph = (uint32_t)(j / C::NST) & 1u;
@@ -128,11 +131,26 @@ __global__ void __launch_bounds__(192, 1)
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_K + s * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
                       bar(B_KFULL + s), a * C::AE, j * C::BN, h, b);
+        k_last[s] = j;
         if (j >= C::NST && !mbar_wait(bar(B_VEMPTY + s), ph ^ 1u, wc)) break;
+        // test hook (fa_sm100_set_debug_flags bit 0): never load the first V tile,
+        // so the MMA issuer's wait for it runs out
+        if ((debug_flags & 1) && j == 0) continue;
         mbar_arrive_expect_tx(bar(B_VFULL + s), C::KV_BYTES);
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_V + s * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
                       bar(B_VFULL + s), a * C::AE, j * C::BN, h, b);
+        v_last[s] = j;
+      }
+      // After an abort, let the loads this CTA issued land before it exits.
+      if (*abort_flag) {
+        mbar_wait_drain(bar(B_QFULL), 0, timeout_ns);
+        for (int s = 0; s < C::NST; ++s) {
+          if (k_last[s] >= 0)
+            mbar_wait_drain(bar(B_KFULL + s), (uint32_t)(k_last[s] / C::NST) & 1u, timeout_ns);
+          if (v_last[s] >= 0)
+            mbar_wait_drain(bar(B_VFULL + s), (uint32_t)(v_last[s] / C::NST) & 1u, timeout_ns);
+        }
       }
     }
   } else if (warp == 5) {
@@ -191,6 +209,7 @@ __global__ void __launch_bounds__(192, 1)
           mma_commit(bar(B_PFREE + pb));
         }
       }
+      mma_commit(bar(B_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
   } else {
     // ------------------------------------------------------------ softmax warps 0..3
@@ -316,6 +335,8 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {
+    if (lane == 0) mbar_wait_drain(bar(B_DRAIN), 0, timeout_ns);
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -330,7 +351,7 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   dim3 grid((a.S + C::BM - 1) / C::BM, a.B * a.H);
   fa_fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
       *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse, a.S, a.H,
-      a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns);
+      a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns, a.debug_flags);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

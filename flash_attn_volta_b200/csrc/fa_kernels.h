@@ -21,6 +21,7 @@ struct FwdArgs {
   int causal;
   int* status;
   unsigned long long timeout_ns;
+  int debug_flags;  // test hooks, see fa_sm100_set_debug_flags
 };
 
 struct BwdArgs {

@@ -91,6 +91,17 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
   }
 }
 
+// Bounded wait used while tearing down after an abort: ignores the abort flag
+// (the point is to let this CTA's own in-flight copies / MMAs finish).
+static __device__ __noinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity,
+                                                    uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w) {
   if (mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, w);

@@ -93,6 +93,12 @@ int fa_sm100_bwd_noalloc(const void* dout, const void* q, const void* k, const v
  * (default 4e9).  Process-wide. */
 void fa_sm100_set_wait_timeout_ns(uint64_t ns);
 
+/* Test hooks, process-wide, 0 in normal use.  Bit 0: the forward kernel skips
+ * loading its first V tile, so an on-device wait runs out (after the wait
+ * timeout), the kernel ORs 1 into the status word and returns; used to test
+ * the timeout path without faulting the GPU.  No counterpart in the reference. */
+void fa_sm100_set_debug_flags(int flags);
+
 const char* fa_sm100_error_string(int code);
 int fa_sm100_abi_version(void);
 

@@ -45,7 +45,7 @@ def _worker(rank, world, port, causal, out_q):
         qs, ks, vs = shard(q), shard(k), shard(v)
         o = ring.ring_flash_attn(qs, ks, vs, causal=causal)
         o.backward(ring.zigzag_shard(do, rank, world))
-        out_q.put((rank, o.detach(), qs.grad, ks.grad, vs.grad))
+        out_q.put((rank,) + tuple(t.detach().cpu().numpy() for t in (o, qs.grad, ks.grad, vs.grad)))
     finally:
         dist.destroy_process_group()
 
@@ -64,7 +64,7 @@ def test_ring_matches_full_attention(world, causal):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    o, dq, dk, dv = (ring.zigzag_unshard([r[i] for r in res]) for i in range(1, 5))
+    o, dq, dk, dv = (ring.zigzag_unshard([torch.from_numpy(r[i]) for r in res]) for i in range(1, 5))
     q, k, v, do = [t.float() for t in make_inputs(2, 64, 2, 16, seed=5)]
     o_ref, _ = attention_fwd(q, k, v, causal, dtype=torch.float64)
     g_ref = attention_bwd(do, q, k, v, causal)

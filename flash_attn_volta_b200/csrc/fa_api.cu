@@ -57,8 +57,11 @@ int check_device() {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool valid_shape(int B, int S, int H, int D) {
+  // grid limits: batch*heads is a grid y extent of the backward's pre/post
+  // kernels (<= 65535); the main kernels use a 1-D grid of heads x blocks
   return B > 0 && S > 0 && H > 0 && (D == 16 || D == 32 || D == 64 || D == 128) &&
-         (long long)B * H < 65536LL * 65535LL;
+         (long long)B * H <= 65535LL &&
+         (long long)B * H * ((S + 127) / 128) <= 2147483647LL;
 }
 
 // Tensor map over a contiguous (B, S, H, D) fp16 tensor; a box is `rows`

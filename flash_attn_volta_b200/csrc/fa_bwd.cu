@@ -45,7 +45,7 @@ namespace fa_sm100 {
 __device__ unsigned long long g_trace[64][16];
 #define TRACE(slot, it)                                                              \
   do {                                                                               \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (it) < 64) g_trace[it][slot] = clock64(); \
+    if (blockIdx.x == 0 && (it) < 64) g_trace[it][slot] = clock64(); \
   } while (0)
 #else
 #define TRACE(slot, it) \
@@ -189,8 +189,11 @@ __global__ void __launch_bounds__(544, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * C_COUNT + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;
-  const int bh = blockIdx.y;
+  // 1-D grid over (head group, key block, head): key block 0 (the most query
+  // tiles under a causal mask) first inside each group of heads
+  const int nkt = (S + C::BN - 1) / C::BN;
+  int bh, kt;
+  grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nkt), nkt, kHeadGroup, bh, kt);
   const int b = bh / H, h = bh % H;
   const int kv0 = kt * C::BN;
   const int ntq = (S + C::BM - 1) / C::BM;
@@ -562,7 +565,7 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   if (cudaFuncSetAttribute(fa_bwd_main_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            C::SMEM) != cudaSuccess)
     return FA_ERR_LAUNCH;
-  dim3 grid((a.S + C::BN - 1) / C::BN, a.B * a.H);
+  dim3 grid(a.B * a.H * ((a.S + C::BN - 1) / C::BN));
   fa_bwd_main_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
       *a.tm_q, *a.tm_do, *a.tm_k, *a.tm_v, a.lse2, a.delta, a.dq_acc, static_cast<__half*>(a.dk),
       static_cast<__half*>(a.dv), a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f,

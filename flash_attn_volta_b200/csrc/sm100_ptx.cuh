@@ -302,6 +302,23 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_ma
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- scheduling
+// Maps a 1-D block index to (batch*head, tile rank) so that heads go in groups
+// of `group` and, inside a group, all heads' rank-0 tiles launch first, then
+// rank 1, ...  Blocks launch in index order, so with rank 0 = the longest tile
+// this is longest-first within each group, while the blocks resident at once
+// touch only one or two groups' K/V (or Q/dO) and share them in L2.
+__device__ __forceinline__ void grid_to_tile(int L, int nbh, int ntile, int group, int& bh,
+                                             int& rank) {
+  const int per_group = group * ntile;
+  const int g = L / per_group;
+  const int rem = L - g * per_group;
+  const int gsize = min(group, nbh - g * group);
+  rank = rem / gsize;
+  bh = g * group + (rem - rank * gsize);
+}
+constexpr int kHeadGroup = 8;
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -313,6 +330,60 @@ __device__ __forceinline__ float lg2(float x) {
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// ---- packed fp32 pairs (Blackwell f32x2 ALU ops)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair, on the FMA pipe instead of the MUFU unit.  Cody-Waite style
+// range reduction: n = round(x) by adding 1.5*2^23 (the integer lands in the low
+// mantissa bits), f = x - n in [-0.5, 0.5]; 2^f by a cubic
+// 1 + c1 f + c2 f^2 + c3 f^3 fitted here to 2^f on [-0.5, 0.5] (relative
+// least squares with iterative reweighting towards minimax); 2^n applied by
+// adding n to the exponent field.  Inputs are clamped to >= -125 (result
+// >= ~2^-125.5, i.e. zero after fp16 rounding).  Max relative error 1.0e-4 over
+// [-125, 8], checked in float32 arithmetic.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x2) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t nmagic = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t t = f2_add(x, magic);
+  const uint64_t r = f2_add(t, nmagic);
+  const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x);
+  uint64_t p = f2_fma(f2_pack(0.05500892549753189f, 0.05500892549753189f), f,
+                      f2_pack(0.24221095442771912f, 0.24221095442771912f));
+  p = f2_fma(p, f, f2_pack(0.6932829022407532f, 0.6932829022407532f));
+  p = f2_fma(p, f, f2_pack(1.f, 1.f));
+  float t0, t1, p0, p1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, p0, p1);
+  const float e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  const float e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return f2_pack(e0, e1);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

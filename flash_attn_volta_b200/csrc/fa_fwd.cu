@@ -7,21 +7,27 @@
 // (B, S, H, D) fp16 tensors (row stride H*D), every head_dim in {16,32,64,128}
 // runs natively (no zero padding), and O is written in (B, S, H, D).
 //
-// One CTA = two 128-row query tiles (t = 0, 1) of one (batch, head) that share
-// every K/V tile.  Warp roles:
-//   warps 0-7 / 8-15  softmax of tile 0 / tile 1: two warps per row quarter,
-//              each owning half of the key columns of its rows (its TMEM lanes);
-//              reads S_t from tensor memory, online softmax in
-//              the exp2 domain, writes P_t (fp16 pairs) back over S_t in
-//              tensor memory, rescales O_t there when the running max grows by
-//              more than 2^8 (lazy rescale); final O/l and LSE epilogue.
-//   warp 16    TMA producer: both Q tiles once, then K/V tiles through a ring.
-//   warps 17,18 MMA issuer of tile 0 / tile 1: S_t = Q_t K_j^T, then, once the
-//              softmax warps have written P_t, O_t += P_t V_j with P_t as the
-//              tensor-memory A operand.  Tile 1 starts half a period after
-//              tile 0, so one tile's MMAs run while the other tile's softmax does.
-// Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D),
-// O1 [256+D, 256+2D); P_t occupies the first 64 columns of S_t.
+// One CTA = one 128-row query tile of one (batch, head).  Tensor memory (512
+// columns): S0 [0,128), S1 [128,256) — S = Q K_j^T double-buffered; P0
+// [256,320), P1 [320,384) — P (fp16 pairs) double-buffered; O [384, 384+D).
+// Because P has its own columns, nothing in the tensor-core stream waits for
+// P to be consumed before the next S is computed.  Warp roles:
+//   warps 0-15  softmax: warp w owns TMEM lane quarter w % 4 (query rows
+//              32*(w%4)..) and key-column quarter w / 4 (32 columns) of each
+//              128-column key tile.  Loads its S columns and releases the S
+//              buffer at once, trades partial row maxima with the other three
+//              warps of its rows (shared memory + a 4-arrival mbarrier),
+//              computes P in the exp2 domain (packed f32x2 arithmetic; one pair
+//              in four on the FMA pipe), writes P to tensor memory and rescales
+//              its share of O when the running max grew by more than 2^8
+//              (lazy rescale); epilogue O/l and LSE.
+//   warp 16    TMA producer: Q once, K and V tiles through separate rings.
+//   warp 17    S issuer:  S_b = Q K_j^T (b = j % 2) once the softmax warps
+//              have read S_b of tile j-2.
+//   warp 18    PV issuer: O += P_b V_j (P_b as the tensor-memory A operand)
+//              once the softmax warps have written P_b.
+// One thread can issue only about one tcgen05.mma per ~90 clk, so the S and PV
+// chains get a thread each; they interleave on the tensor core.
 //
 // Semantics kept from the reference: top-left causal mask (column > row is
 // masked, triton_fa.py:124-126), columns >= S masked (:123), LSE = m + ln(l)
@@ -39,12 +45,12 @@ namespace fa_sm100 {
 #ifndef FA_TRACE_BLOCK
 #define FA_TRACE_BLOCK 0
 #endif
-// Debug build only: clock64() stamps of barrier events of CTA (0, 0), read back
+// Debug build only: clock64() stamps of barrier events of one CTA, read back
 // with fa_debug_trace_fwd().
 __device__ unsigned long long g_ftrace[64][16];
-#define FTRACE(slot, it)                                                              \
-  do {                                                                                \
-    if (blockIdx.x == FA_TRACE_BLOCK && (it) < 64) g_ftrace[it][slot] = clock64(); \
+#define FTRACE(slot, it)                                                                    \
+  do {                                                                                      \
+    if (blockIdx.x == FA_TRACE_BLOCK && (it) < 64) g_ftrace[it][slot] = clock64();           \
   } while (0)
 #else
 #define FTRACE(slot, it) \
@@ -54,40 +60,43 @@ __device__ unsigned long long g_ftrace[64][16];
 
 template <int D>
 struct FwdCfg {
-  static constexpr int BM = 128, BN = 128, NT = 2;  // query tile rows, key tile rows, tiles
+  static constexpr int BM = 128, BN = 128;  // query rows per CTA, key rows per tile
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle width (bytes)
   static constexpr int AE = SWB / 2;                        // elements per swizzle row
   static constexpr int NAT = D / AE;                        // swizzle atoms along D
-  static constexpr int NST = (D == 128) ? 2 : 3;            // K/V ring depth
+  static constexpr int NSTK = (D == 128) ? 3 : 4;           // K ring depth
+  static constexpr int NSTV = (D == 128) ? 2 : 4;           // V ring depth
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + NST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NST * KV_BYTES;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + NSTK * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NSTV * KV_BYTES;
+  static constexpr int BAR_BYTES = 512;  // barriers, TMEM slot, abort flag
   static constexpr int OFF_XCH = OFF_BAR + BAR_BYTES;  // row-max / row-sum exchange
-  static constexpr int SMEM = OFF_XCH + 2 * 2 * 2 * 128 * 4 + 1024;  // + alignment slack
+  static constexpr int XCH_BYTES = 2 * 4 * 128 * 4;    // [parity][column quarter][row]
+  static constexpr int SMEM = OFF_XCH + XCH_BYTES + 1024;  // + alignment slack
   static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr int THREADS = 608;
   static constexpr uint32_t TMEM_COLS = 512;
-  __host__ __device__ static constexpr uint32_t col_s(int t) { return (uint32_t)t * 128u; }
-  __host__ __device__ static constexpr uint32_t col_o(int t) { return 256u + (uint32_t)t * D; }
+  static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // S_b: +128 b, P_b: +64 b
 };
 
 // barrier slots (8 bytes each) inside the barrier block
 enum FwdBar {
   B_QFULL = 0,
-  B_KFULL = 1,    // +NST (<= 3)
-  B_KEMPTY = 4,   // +NST, one commit per active tile
-  B_VFULL = 7,    // +NST
-  B_VEMPTY = 10,  // +NST, one commit per active tile
-  B_SFULL = 13,   // +tile
-  B_PFULL = 15,   // +tile, 4 arrivals (softmax warps of the tile)
-  B_ODONE = 17,   // +tile
-  B_DRAIN = 19,   // 2 arrivals: each issuer's last commit
-  B_XCHG = 20,    // +4*tile+quarter: 2 arrivals (the two halves of a row quarter)
-  B_COUNT = 28
+  B_KFULL = 1,    // +NSTK (<= 4)
+  B_KEMPTY = 5,   // +NSTK
+  B_VFULL = 9,    // +NSTV (<= 4)
+  B_VEMPTY = 13,  // +NSTV
+  B_SFULL = 17,   // +b
+  B_SFREE = 19,   // +b, 16 arrivals: softmax warps hold S_b in registers
+  B_PFULL = 21,   // +b, 16 arrivals: P_b written (and O rescaled)
+  B_PFREE = 23,   // +b: O += P_b V done reading P_b
+  B_ODONE = 25,   // every O += P V (waited only where at most one phase is pending)
+  B_XCHG = 26,    // +row quarter, 4 arrivals
+  B_DRAIN = 30,   // 2 arrivals: each issuer's last commit
+  B_COUNT = 31
 };
 
 template <int D>
@@ -107,33 +116,24 @@ __global__ void __launch_bounds__(608, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * B_COUNT + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // 1-D grid over (head group, tile rank, head): longest blocks first inside
-  // each group of heads, K/V of only a few heads live at once (L2 reuse)
-  const int nblk = (S + C::NT * C::BM - 1) / (C::NT * C::BM);
+  // 1-D grid over (head group, query block rank, head): longest blocks first
+  // inside each group of heads, K/V of only a few heads live at once (L2 reuse)
+  const int nblk = (S + C::BM - 1) / C::BM;
   int bh, rank;
   grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nblk), nblk, kHeadGroup, bh, rank);
-  const int blk = causal ? (nblk - 1 - rank) : rank;
+  const int qt = causal ? (nblk - 1 - rank) : rank;
   const int b = bh / H, h = bh % H;
-  const int q0 = blk * C::NT * C::BM;
+  const int q0 = qt * C::BM;
   const int nkv_all = (S + C::BN - 1) / C::BN;
-  int nkv_t[C::NT];
-#pragma unroll
-  for (int t = 0; t < C::NT; ++t) {
-    const int qt = q0 + t * C::BM;
-    nkv_t[t] = qt >= S ? 0 : (causal ? min(nkv_all, (qt + C::BM + C::BN - 1) / C::BN) : nkv_all);
-  }
-  const int n_active = (nkv_t[0] > 0) + (nkv_t[1] > 0);
-  const int nkv = max(nkv_t[0], nkv_t[1]);
+  const int nkv = causal ? min(nkv_all, (q0 + C::BM + C::BN - 1) / C::BN) : nkv_all;
 
   WaitCtx wc{abort_flag, status, timeout_ns};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < B_COUNT; ++i) {
       uint32_t cnt = 1;
-      if ((i >= B_KEMPTY && i < B_KEMPTY + 3) || (i >= B_VEMPTY && i < B_VEMPTY + 3))
-        cnt = (uint32_t)n_active;
-      if (i == B_PFULL || i == B_PFULL + 1) cnt = 8;
-      if (i >= B_XCHG) cnt = 2;
+      if (i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1) cnt = 16;
+      if (i >= B_XCHG && i < B_XCHG + 4) cnt = 4;
       if (i == B_DRAIN) cnt = 2;
       mbar_init(bar(i), cnt);
     }
@@ -155,161 +155,150 @@ __global__ void __launch_bounds__(608, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar(B_QFULL), C::NT * C::Q_BYTES);
-      for (int t = 0; t < C::NT; ++t)
-        for (int a = 0; a < C::NAT; ++a)
-          tma_load_4d(sbase + C::OFF_Q + t * C::Q_BYTES + a * C::BM * C::SWB, &tm_q, bar(B_QFULL),
-                      a * C::AE, q0 + t * C::BM, h, b);
-      int k_last[C::NST], v_last[C::NST];  // last tile index loaded into each stage
-      for (int s = 0; s < C::NST; ++s) k_last[s] = v_last[s] = -1;
+      mbar_arrive_expect_tx(bar(B_QFULL), C::Q_BYTES);
+      for (int a = 0; a < C::NAT; ++a)
+        tma_load_4d(sbase + C::OFF_Q + a * C::BM * C::SWB, &tm_q, bar(B_QFULL), a * C::AE, q0, h,
+                    b);
+      int k_last[C::NSTK], v_last[C::NSTV];  // last tile index loaded into each slot
+      for (int s = 0; s < C::NSTK; ++s) k_last[s] = -1;
+      for (int s = 0; s < C::NSTV; ++s) v_last[s] = -1;
       for (int j = 0; j < nkv; ++j) {
-        const int s = j % C::NST;
-        const uint32_t ph = (uint32_t)(j / C::NST) & 1u;
-        if (j >= C::NST && !mbar_wait(bar(B_KEMPTY + s), ph ^ 1u, wc)) break;
-        mbar_arrive_expect_tx(bar(B_KFULL + s), C::KV_BYTES);
+        const int sk = j % C::NSTK, sv = j % C::NSTV;
+        if (j >= C::NSTK &&
+            !mbar_wait(bar(B_KEMPTY + sk), (uint32_t)(j / C::NSTK - 1) & 1u, wc))
+          break;
+        mbar_arrive_expect_tx(bar(B_KFULL + sk), C::KV_BYTES);
         for (int a = 0; a < C::NAT; ++a)
-          tma_load_4d(sbase + C::OFF_K + s * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
-                      bar(B_KFULL + s), a * C::AE, j * C::BN, h, b);
-        k_last[s] = j;
-        if (j >= C::NST && !mbar_wait(bar(B_VEMPTY + s), ph ^ 1u, wc)) break;
+          tma_load_4d(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
+                      bar(B_KFULL + sk), a * C::AE, j * C::BN, h, b);
+        k_last[sk] = j;
+        if (j >= C::NSTV &&
+            !mbar_wait(bar(B_VEMPTY + sv), (uint32_t)(j / C::NSTV - 1) & 1u, wc))
+          break;
         // test hook (fa_sm100_set_debug_flags bit 0): never load the first V tile,
-        // so the MMA issuers' wait for it runs out
+        // so the PV issuer's wait for it runs out
         if ((debug_flags & 1) && j == 0) continue;
-        mbar_arrive_expect_tx(bar(B_VFULL + s), C::KV_BYTES);
+        mbar_arrive_expect_tx(bar(B_VFULL + sv), C::KV_BYTES);
         for (int a = 0; a < C::NAT; ++a)
-          tma_load_4d(sbase + C::OFF_V + s * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
-                      bar(B_VFULL + s), a * C::AE, j * C::BN, h, b);
-        v_last[s] = j;
+          tma_load_4d(sbase + C::OFF_V + sv * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
+                      bar(B_VFULL + sv), a * C::AE, j * C::BN, h, b);
+        v_last[sv] = j;
       }
       // After an abort, let the loads this CTA issued land before it exits.
       if (*abort_flag) {
         mbar_wait_drain(bar(B_QFULL), 0, timeout_ns);
-        for (int s = 0; s < C::NST; ++s) {
+        for (int s = 0; s < C::NSTK; ++s)
           if (k_last[s] >= 0)
-            mbar_wait_drain(bar(B_KFULL + s), (uint32_t)(k_last[s] / C::NST) & 1u, timeout_ns);
+            mbar_wait_drain(bar(B_KFULL + s), (uint32_t)(k_last[s] / C::NSTK) & 1u, timeout_ns);
+        for (int s = 0; s < C::NSTV; ++s)
           if (v_last[s] >= 0)
-            mbar_wait_drain(bar(B_VFULL + s), (uint32_t)(v_last[s] / C::NST) & 1u, timeout_ns);
-        }
+            mbar_wait_drain(bar(B_VFULL + s), (uint32_t)(v_last[s] / C::NSTV) & 1u, timeout_ns);
       }
     }
-  } else if (warp >= 17) {
-    // ------------------------------------------------------------ MMA issuers (one per tile)
-    const int t = warp - 17;
+  } else if (warp == 17) {
+    // ------------------------------------------------------------ S issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(C::BM, C::BN, false, false);
-      constexpr uint32_t idesc_pv = make_idesc_f16(C::BM, D, false, true);
       constexpr uint32_t swz = swizzle_field(C::SWB);
-      const uint32_t d_s = tmem + C::col_s(t);
-      const uint32_t d_o = tmem + C::col_o(t);
-      const uint32_t qb = sbase + C::OFF_Q + t * C::Q_BYTES;
-      bool ok = nkv_t[t] > 0 && mbar_wait(bar(B_QFULL), 0, wc);
-      for (int j = 0; ok && j < nkv_t[t]; ++j) {
-        const int s = j % C::NST;
-        const uint32_t ph = (uint32_t)(j / C::NST) & 1u;
-        // S_t(j) overwrites the TMEM columns that P_t(j-1) occupies; it is issued
-        // by this same thread after O_t += P_t(j-1) V, and tcgen05.mma operations
-        // of one thread execute in issue order, so no wait is needed here.
-        if (!mbar_wait(bar(B_KFULL + s), ph, wc)) break;
-        // Tile 1 starts once tile 0's first softmax is done: the two tiles then run
-        // half a period apart, so one tile's MMAs overlap the other's softmax.
-        if (t == 1 && j == 0 && nkv_t[0] > 0 && !mbar_wait(bar(B_PFULL + 0), 0u, wc)) break;
-        FTRACE(0 + 4 * t, j);
+      bool ok = mbar_wait(bar(B_QFULL), 0, wc);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int sk = j % C::NSTK, sb = j & 1;
+        if (!mbar_wait(bar(B_KFULL + sk), (uint32_t)(j / C::NSTK) & 1u, wc) ||
+            (j >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)))
+          break;
+        FTRACE(0, j);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int a = (kk * 16) / C::AE;
           const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
-          const uint64_t ad =
-              make_smem_desc(qb + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
+          const uint64_t ad = make_smem_desc(sbase + C::OFF_Q + a * C::BM * C::SWB + koff, 16,
+                                             8 * C::SWB, swz);
           const uint64_t bd =
-              make_smem_desc(sbase + C::OFF_K + s * C::KV_BYTES + a * C::BN * C::SWB + koff, 16,
+              make_smem_desc(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB + koff, 16,
                              8 * C::SWB, swz);
-          mma_f16_ss(d_s, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + C::COL_S + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(B_SFULL + t));
-        mma_commit(bar(B_KEMPTY + s));
-        FTRACE(1 + 4 * t, j);
-        if (!mbar_wait(bar(B_PFULL + t), (uint32_t)j & 1u, wc) ||
-            !mbar_wait(bar(B_VFULL + s), ph, wc))
-          break;
-        FTRACE(2 + 4 * t, j);
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t bd = make_smem_desc(sbase + C::OFF_V + s * C::KV_BYTES + kk * 16 * C::SWB,
-                                             C::BN * C::SWB, 8 * C::SWB, swz);
-          mma_f16_ts(d_o, d_s + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar(B_ODONE + t));
-        mma_commit(bar(B_VEMPTY + s));
-        FTRACE(3 + 4 * t, j);
+        mma_commit(bar(B_SFULL + sb));
+        mma_commit(bar(B_KEMPTY + sk));
+        FTRACE(1, j);
       }
       mma_commit(bar(B_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
+  } else if (warp == 18) {
+    // ------------------------------------------------------------ PV issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_pv = make_idesc_f16(C::BM, D, false, true);
+      constexpr uint32_t swz = swizzle_field(C::SWB);
+      bool ok = true;
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int sv = j % C::NSTV, pb = j & 1;
+        if (!mbar_wait(bar(B_PFULL + pb), (uint32_t)(j >> 1) & 1u, wc) ||
+            !mbar_wait(bar(B_VFULL + sv), (uint32_t)(j / C::NSTV) & 1u, wc))
+          break;
+        FTRACE(2, j);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t bd = make_smem_desc(sbase + C::OFF_V + sv * C::KV_BYTES + kk * 16 * C::SWB,
+                                             C::BN * C::SWB, 8 * C::SWB, swz);
+          mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + pb * 64 + kk * 8, bd, idesc_pv,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(B_ODONE));
+        mma_commit(bar(B_VEMPTY + sv));
+        mma_commit(bar(B_PFREE + pb));
+        FTRACE(3, j);
+      }
+      mma_commit(bar(B_DRAIN));
+    }
   } else {
     // ------------------------------------------------------------ softmax warps 0..15
-    // Tile t = warp / 8; inside a tile, warp w owns TMEM lane quarter w % 4 (rows
-    // 32*(w%4)..) and half hh of each key tile's 128 columns.  The two halves of a
-    // row trade partial row maxima through shared memory every step (a 2-arrival
-    // mbarrier per row quarter, bounded wait) and add their row sums at the end.
-    const int t = warp >> 3;
-    const int hh = (warp >> 2) & 1;
-    const int lq = warp & 3;
-    const int r = lq * 32 + lane;  // query row inside the tile == TMEM lane
-    const int q_tile0 = q0 + t * C::BM;
-    const int q_idx = q_tile0 + r;
+    const int lq = warp & 3;  // TMEM lane quarter (query rows 32*lq..)
+    const int cq = warp >> 2;  // key-column quarter (32 columns of each key tile)
+    const int r = lq * 32 + lane;
+    const int q_idx = q0 + r;
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + C::col_s(t);
-    const uint32_t o_addr = tmem + lane_base + C::col_o(t);
-    constexpr int HC = C::BN / 2;                   // columns per half
-    constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // O columns per half
-    const bool o_cols = hh * EC < D;
-    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);  // [2][2 tiles][2 halves][128]
-    auto xslot = [&](int par, int half) { return xch + ((par * 2 + t) * 2 + half) * 128 + r; };
-    const uint32_t xbar = bar(B_XCHG + t * 4 + lq);
+    constexpr int QC = C::BN / 4;                   // key columns per warp
+    constexpr int EC = (D / 4 >= 16) ? D / 4 : 16;  // O columns per warp
+    const bool o_cols = cq * EC < D;
+    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);  // [parity][cq][row]
+    const uint32_t xbar = bar(B_XCHG + lq);
     const float NEG_INF = -__int_as_float(0x7f800000);
     float m_run = NEG_INF;  // running max, already multiplied by scale*log2(e)
-    float l_run = 0.f;      // this half's share of the row sum
+    float l_run = 0.f;      // this warp's share of the row sum
     bool ok = true;
-    const int nk = nkv_t[t];
-    for (int j = 0; j < nk; ++j) {
-      if (!mbar_wait(bar(B_SFULL + t), (uint32_t)j & 1u, wc)) { ok = false; break; }
-      // The two tiles' softmaxes take turns (tile 1's step j after tile 0's step
-      // j, tile 0's step j after tile 1's step j-1): each runs alone on the exp2
-      // unit while the tensor core works on the other tile.
-      if (t == 1 && j < nkv_t[0] && !mbar_wait(bar(B_PFULL + 0), (uint32_t)j & 1u, wc)) {
-        ok = false;
-        break;
-      }
-      if (t == 0 && j > 0 && j - 1 < nkv_t[1] &&
-          !mbar_wait(bar(B_PFULL + 1), (uint32_t)(j - 1) & 1u, wc)) {
-        ok = false;
-        break;
-      }
-      if (r == 0 && hh == 0) FTRACE(8 + 4 * t, j);
+    for (int j = 0; j < nkv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(bar(B_SFULL + sb), (uint32_t)(j >> 1) & 1u, wc)) { ok = false; break; }
+      if (threadIdx.x == 0) FTRACE(8, j);
       tc_fence_after();
-      float sv[HC];
-      tmem_ld32(s_addr + hh * HC, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld32(s_addr + hh * HC + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      float sv[QC];
+      tmem_ld32(tmem + lane_base + C::COL_S + sb * 128 + cq * QC,
+                *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
       tmem_wait_ld();
-      const int kv0 = j * C::BN + hh * HC;
-      const bool need_mask = (kv0 + HC > S) || (causal && kv0 + HC - 1 > q_tile0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_SFREE + sb));
+      const int kv0 = j * C::BN + cq * QC;
+      const bool need_mask = (kv0 + QC > S) || (causal && kv0 + QC - 1 > q0);
       if (need_mask) {
-        const int lim = min(S - kv0, causal ? (q_idx - kv0 + 1) : HC);
+        const int lim = min(S - kv0, causal ? (q_idx - kv0 + 1) : QC);
 #pragma unroll
-        for (int c = 0; c < HC; ++c)
+        for (int c = 0; c < QC; ++c)
           if (c >= lim) sv[c] = NEG_INF;
       }
       float mt = fmax3(sv[0], sv[1], sv[2]);
 #pragma unroll
-      for (int c = 3; c < HC - 1; c += 2) mt = fmax3(mt, sv[c], sv[c + 1]);
-      mt = fmaxf(mt, sv[HC - 1]);
-      // row max over both halves
-      *xslot(j & 1, hh) = mt;
+      for (int c = 3; c < QC - 1; c += 2) mt = fmax3(mt, sv[c], sv[c + 1]);
+      mt = fmaxf(mt, sv[QC - 1]);
+      // row max over the four column quarters
+      float* xs = xch + (j & 1) * 512;
+      xs[cq * 128 + r] = mt;
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
       if (!mbar_wait(xbar, (uint32_t)j & 1u, wc)) { ok = false; break; }
-      mt = fmaxf(mt, *xslot(j & 1, hh ^ 1));
+      mt = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
       const float m_new = fmaxf(m_run, mt * scale_log2);
       // Lazy rescale: keep the old reference max unless the row max grew by > 8
       // (a factor 256 in P), or this is the first finite max of the row.
@@ -323,9 +312,9 @@ __global__ void __launch_bounds__(608, 1)
       const uint64_t c2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
       uint64_t sum2 = f2_pack(0.f, 0.f);
-      uint32_t pp[HC / 2];
+      uint32_t pp[QC / 2];
 #pragma unroll
-      for (int k = 0; k < HC / 2; ++k) {
+      for (int k = 0; k < QC / 2; ++k) {
         const uint64_t x2 = f2_fma(f2_pack(sv[2 * k], sv[2 * k + 1]), c2, nm2);
         uint64_t p2;
         if ((k & 3) == 3) {
@@ -343,18 +332,23 @@ __global__ void __launch_bounds__(608, 1)
       float lsum0, lsum1;
       f2_unpack(sum2, lsum0, lsum1);
       l_run = l_run * alpha + (lsum0 + lsum1);
-      if (r == 0 && hh == 0) FTRACE(9 + 4 * t, j);
-      // P_t (fp16 pairs) over the first 64 columns of S_t: A operand of O_t += P_t V
-      tmem_st32(s_addr + hh * (HC / 2), pp);
-      // Rescaling O_t needs O_t += P_t V_{j-1} to have completed (rare: lazy rescale)
+      if (threadIdx.x == 0) FTRACE(9, j);
+      // P_b is free once O += P_b V of tile j-2 has read it
+      if (j >= 2 && !mbar_wait(bar(B_PFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_st16(tmem + lane_base + C::COL_P + sb * 64 + cq * (QC / 2), pp);
+      // Rescaling O needs O += P V of tile j-1 to have completed (rare: lazy rescale)
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        if (!mbar_wait(bar(B_ODONE + t), (uint32_t)(j - 1) & 1u, wc)) { ok = false; break; }
+        if (!mbar_wait(bar(B_ODONE), (uint32_t)(j - 1) & 1u, wc)) { ok = false; break; }
         tc_fence_after();
         if (o_cols) {
 #pragma unroll
           for (int c = 0; c < EC / 16; ++c) {
             uint32_t o[16];
-            const uint32_t ta = o_addr + hh * EC + c * 16;
+            const uint32_t ta = tmem + lane_base + C::COL_O + cq * EC + c * 16;
             tmem_ld16(ta, o);
             tmem_wait_ld();
 #pragma unroll
@@ -366,29 +360,35 @@ __global__ void __launch_bounds__(608, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PFULL + t));
-      if (r == 0 && hh == 0) FTRACE(10 + 4 * t, j);
+      if (lane == 0) mbar_arrive(bar(B_PFULL + sb));
+      if (threadIdx.x == 0) FTRACE(10, j);
       m_run = m_use;
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && nk > 0) {
-      // the full row sum: this half's plus the other half's
-      *xslot(nk & 1, hh) = l_run;
+    if (ok && nkv > 0) {
+      // the full row sum: the four column quarters' shares
+      float* xs = xch + (nkv & 1) * 512;
+      xs[cq * 128 + r] = l_run;
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
-      ok = mbar_wait(xbar, (uint32_t)nk & 1u, wc);
-      if (ok) l_run += *xslot(nk & 1, hh ^ 1);
+      ok = mbar_wait(xbar, (uint32_t)nkv & 1u, wc);
+      if (ok) l_run = (xs[r] + xs[128 + r]) + (xs[256 + r] + xs[384 + r]);
     }
-    if (ok && nk > 0 && mbar_wait(bar(B_ODONE + t), (uint32_t)(nk - 1) & 1u, wc)) {
+    // Wait for the last O += P V.  Its P-buffer barrier is unambiguous here (this
+    // thread observed that buffer's previous phase), unlike the every-PV ODONE
+    // barrier, which may still be two phases behind; a commit covers all of the
+    // issuing thread's earlier MMAs.
+    if (ok && nkv > 0 &&
+        mbar_wait(bar(B_PFREE + ((nkv - 1) & 1)), (uint32_t)((nkv - 1) >> 1) & 1u, wc)) {
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = q_idx < S;
-      __half* orow = out + (((size_t)b * S + q_idx) * H + h) * D + hh * EC;
+      __half* orow = out + (((size_t)b * S + q_idx) * H + h) * D + cq * EC;
       if (o_cols) {
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
           uint32_t o[16];
-          tmem_ld16(o_addr + hh * EC + c * 16, o);
+          tmem_ld16(tmem + lane_base + C::COL_O + cq * EC + c * 16, o);
           tmem_wait_ld();
           uint4 w0, w1;
           w0.x = pack_half2(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(608, 1)
           }
         }
       }
-      if (lse != nullptr && row_ok && hh == 0) {
+      if (lse != nullptr && row_ok && cq == 0) {
         const float m_safe = (m_run == NEG_INF) ? 0.f : m_run;
         lse[(size_t)bh * S + q_idx] =
             l_run > 0.f ? (m_safe + lg2(l_run)) * 0.69314718055994530942f : __int_as_float(0x7f800000);
@@ -430,7 +430,7 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   if (cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            C::SMEM) != cudaSuccess)
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.H * ((a.S + C::NT * C::BM - 1) / (C::NT * C::BM)));
+  dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
   fa_fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
       *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse, a.S, a.H,
       a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns, a.debug_flags);
@@ -450,9 +450,6 @@ int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
 }  // namespace fa_sm100
 
 #ifdef FA_FWD_TRACE
-#ifndef FA_TRACE_BLOCK
-#define FA_TRACE_BLOCK 0
-#endif
 extern "C" int fa_debug_trace_fwd(void* dst) {
   return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_ftrace, sizeof(fa_sm100::g_ftrace));
 }

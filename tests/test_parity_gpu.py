@@ -200,3 +200,22 @@ def test_empty_sequence():
     assert o.shape == q.shape and lse.shape == (2, 3, 0)
     dq, dk, dv = flash_attn_backward(q, q, q, q, o, lse)
     assert dq.shape == q.shape
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_repeated_runs_bit_identical(causal):
+    """Intermittent ordering bugs show up as run-to-run differences: the forward
+    (O, LSE) and dK / dV (no atomics) must be bit-identical across runs."""
+    from flash_attn_volta_b200 import flash_attn, flash_attn_forward
+    q, k, v, do = [t.to(DEV) for t in make_inputs(2, 1024, 8, 64, seed=31)]
+    ref = None
+    for _ in range(8):
+        o, lse = flash_attn_forward(q, k, v, causal=causal, return_softmax_lse=True)
+        kk, vv = k.clone().requires_grad_(), v.clone().requires_grad_()
+        flash_attn(q, kk, vv, causal=causal).backward(do)
+        cur = (o, lse, kk.grad, vv.grad)
+        if ref is None:
+            ref = cur
+        else:
+            for a, b in zip(ref, cur):
+                assert torch.equal(a, b)

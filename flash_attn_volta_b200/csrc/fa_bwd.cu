@@ -381,65 +381,67 @@ __global__ void __launch_bounds__(544, 1)
       }
       if (threadIdx.x == 0) TRACE(7, i);
       tc_fence_after();
-      uint32_t sr[HW], dr[HW];
-#pragma unroll
-      for (int c = 0; c < HW / 32; ++c) {
-        tmem_ld32(tmem + lane_base + C::COL_S + c0 + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-        tmem_ld32(tmem + lane_base + C::COL_DP + c0 + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&dr[c * 32]));
-      }
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C_SFREE));
-      if (threadIdx.x == 0) TRACE(8, i);
       const float* lse_s = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * C::BM * 4);
       const float* del_s = reinterpret_cast<const float*>(smem + C::OFF_DELTA + st * C::BM * 4);
-      // P^T and dS^T for this thread's HW query columns, packed to fp16 pairs
-      uint32_t pp[HW / 2], dd[HW / 2];
-#pragma unroll
-      for (int e = 0; e < HW; e += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + c0 + e);
-        const float4 d4 = *reinterpret_cast<const float4*>(del_s + c0 + e);
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-        const float dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-        float p4[4], ds4[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int ql = c0 + e + u;
-          const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
-          const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lv[u])) : 0.f;
-          p4[u] = pe;
-          ds4[u] = pe * (__uint_as_float(dr[e + u]) - dv4[u]);
+      // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
+      // dP^T are released after the last chunk's loads; P^T / dS^T are written only
+      // once the previous tile's dV / dK MMAs have read them (PFREE).
+#pragma unroll 1
+      for (int cc = 0; cc < HW / 32; ++cc) {
+        const int cb = c0 + cc * 32;  // first query column of this chunk
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
+        tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
+        tmem_wait_ld();
+        if (cc == HW / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_SFREE));
+          if (threadIdx.x == 0) TRACE(8, i);
         }
-        pp[e / 2] = pack_half2(p4[0], p4[1]);
-        pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
-        dd[e / 2] = pack_half2(ds4[0], ds4[1]);
-        dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
-      }
-      if (threadIdx.x == 0) TRACE(11, i);
-      if (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc)) {
-        ok = false;
-        break;
-      }
-      if (threadIdx.x == 0) TRACE(9, i);
-      // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
-      // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
-      if constexpr (HW == 32) {
-        tmem_st16(tmem + lane_base + C::COL_PT + c0 / 2, pp);
-        if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + c0 / 2, dd);
-      } else {
-        tmem_st32(tmem + lane_base + C::COL_PT + c0 / 2, pp);
-        if constexpr (C::DS_TMEM) tmem_st32(tmem + lane_base + C::COL_DST + c0 / 2, dd);
-      }
-      const int a = c0 / 64;
-      const int ch0 = (c0 % 64) / 8;
-      const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+        // P^T and dS^T for these 32 query columns, packed to fp16 pairs
+        uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int u = 0; u < HW / 8; ++u)
-        st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
-                     dd[4 * u + 3]);
+        for (int e = 0; e < 32; e += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lse_s + cb + e);
+          const float4 d4 = *reinterpret_cast<const float4*>(del_s + cb + e);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+          float p4[4], ds4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int ql = cb + e + u;
+            const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
+            const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lv[u])) : 0.f;
+            p4[u] = pe;
+            ds4[u] = pe * (__uint_as_float(dr[e + u]) - dv4[u]);
+          }
+          pp[e / 2] = pack_half2(p4[0], p4[1]);
+          pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
+          dd[e / 2] = pack_half2(ds4[0], ds4[1]);
+          dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
+        }
+        if (cc == 0) {
+          if (threadIdx.x == 0) TRACE(11, i);
+          if (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc)) {
+            ok = false;
+            break;
+          }
+          if (threadIdx.x == 0) TRACE(9, i);
+        }
+        // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
+        // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
+        tmem_st16(tmem + lane_base + C::COL_PT + cb / 2, pp);
+        if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + cb / 2, dd);
+        const int a = cb / 64;
+        const int ch0 = (cb % 64) / 8;
+        const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
+                       dd[4 * u + 3]);
+      }
+      if (!ok) break;
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -511,30 +513,38 @@ __global__ void __launch_bounds__(544, 1)
         for (int e = 0; e < 32; ++e)
           st_shared_f32(stage + (uint32_t)((32 + e) * D + d) * 4u, __uint_as_float(v1[e]));
       } else {
-        // TMEM lane = query row, column = d
+        // TMEM lane = query row, column = d; CW columns at a time (flat register
+        // use). The staging buffer must be free before the first chunk's stores;
+        // the accumulator is released after the last chunk's loads.
+        constexpr int CW = D < 32 ? D : 32;
+        constexpr int NP = CW / 4;  // 16-byte pieces per chunk row
         const int qr = wq * 32 + lane;
-        uint32_t v[D];
-#pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          tmem_ld16(tmem + lane_base + C::COL_DQ + c * 16,
-                    *reinterpret_cast<uint32_t(*)[16]>(&v[c * 16]));
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(C_DQFREE));
-        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();
+        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
         named_bar_sync(1, 128);
         const uint32_t rowa = stage + (uint32_t)(qr * D * 4);
 #pragma unroll
-        for (int c = 0; c < D / 4; ++c) {
-          const int cc = (c + lane) % (D / 4);  // rotate chunks across lanes: no bank conflicts
-          uint32_t w0 = v[4 * c], w1 = v[4 * c + 1], w2 = v[4 * c + 2], w3 = v[4 * c + 3];
-          // select the rotated chunk without dynamic register indexing
+        for (int c = 0; c < D / CW; ++c) {
+          uint32_t v[CW];
+          if constexpr (CW == 32)
+            tmem_ld32(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[32]>(v));
+          else
+            tmem_ld16(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[16]>(v));
+          tmem_wait_ld();
+          if (c == D / CW - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(C_DQFREE));
+          }
 #pragma unroll
-          for (int t = 0; t < D / 4; ++t)
-            if (t == cc) { w0 = v[4 * t]; w1 = v[4 * t + 1]; w2 = v[4 * t + 2]; w3 = v[4 * t + 3]; }
-          st_shared_v4(rowa + (uint32_t)cc * 16u, w0, w1, w2, w3);
+          for (int p = 0; p < NP; ++p) {
+            const int pc = (p + lane) % NP;  // rotate pieces across lanes: fewer bank conflicts
+            uint32_t w0 = v[0], w1 = v[1], w2 = v[2], w3 = v[3];
+            // select the rotated piece without dynamic register indexing
+#pragma unroll
+            for (int t = 0; t < NP; ++t)
+              if (t == pc) { w0 = v[4 * t]; w1 = v[4 * t + 1]; w2 = v[4 * t + 2]; w3 = v[4 * t + 3]; }
+            st_shared_v4(rowa + (uint32_t)(c * CW + 4 * pc) * 4u, w0, w1, w2, w3);
+          }
         }
       }
       fence_proxy_async_smem();

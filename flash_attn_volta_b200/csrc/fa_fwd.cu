@@ -21,7 +21,8 @@
 //              in four on the FMA pipe), writes P to tensor memory and rescales
 //              its share of O when the running max grew by more than 2^8
 //              (lazy rescale); epilogue O/l and LSE.
-//   warp 16    TMA producer: Q once, K and V tiles through separate rings.
+//   warp 16    TMA producer: Q once, then K tiles through their ring.
+//   warp 19    TMA producer: V tiles through their ring.
 //   warp 17    S issuer:  S_b = Q K_j^T (b = j % 2) once the softmax warps
 //              have read S_b of tile j-2.
 //   warp 18    PV issuer: O += P_b V_j (P_b as the tensor-memory A operand)
@@ -77,7 +78,7 @@ struct FwdCfg {
   static constexpr int XCH_BYTES = 2 * 4 * 128 * 4;    // [parity][column quarter][row]
   static constexpr int SMEM = OFF_XCH + XCH_BYTES + 1024;  // + alignment slack
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 608;
+  static constexpr int THREADS = 640;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // S_b: +128 b, P_b: +64 b
 };
@@ -100,7 +101,7 @@ enum FwdBar {
 };
 
 template <int D>
-__global__ void __launch_bounds__(608, 1)
+__global__ void __launch_bounds__(640, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
                   float* __restrict__ lse, int S, int H, float scale_log2, int causal, int* status,
@@ -150,20 +151,20 @@ __global__ void __launch_bounds__(608, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 16) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer: Q, K
+    // K runs ahead on its own ring: were K and V issued by one thread, each K
+    // load would queue behind a V slot that frees only when O += P V of two
+    // tiles back completes, about one load latency before S needs that K.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(bar(B_QFULL), C::Q_BYTES);
       for (int a = 0; a < C::NAT; ++a)
         tma_load_4d(sbase + C::OFF_Q + a * C::BM * C::SWB, &tm_q, bar(B_QFULL), a * C::AE, q0, h,
                     b);
-      int k_last[C::NSTK], v_last[C::NSTV];  // last tile index loaded into each slot
-      for (int s = 0; s < C::NSTK; ++s) k_last[s] = -1;
-      for (int s = 0; s < C::NSTV; ++s) v_last[s] = -1;
+      int loaded = 0;
       for (int j = 0; j < nkv; ++j) {
-        const int sk = j % C::NSTK, sv = j % C::NSTV;
+        const int sk = j % C::NSTK;
         if (j >= C::NSTK &&
             !mbar_wait(bar(B_KEMPTY + sk), (uint32_t)(j / C::NSTK - 1) & 1u, wc))
           break;
@@ -171,10 +172,26 @@ __global__ void __launch_bounds__(608, 1)
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
                       bar(B_KFULL + sk), a * C::AE, j * C::BN, h, b);
-        k_last[sk] = j;
+        loaded = j + 1;
+      }
+      // After an abort, let the loads this thread issued land before the CTA exits.
+      if (*abort_flag) {
+        mbar_wait_drain(bar(B_QFULL), 0, timeout_ns);
+        for (int j = max(0, loaded - C::NSTK); j < loaded; ++j)
+          mbar_wait_drain(bar(B_KFULL + j % C::NSTK), (uint32_t)(j / C::NSTK) & 1u, timeout_ns);
+      }
+    }
+  } else if (warp == 19) {
+    // ------------------------------------------------------------ TMA producer: V
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_v);
+      int loaded = 0;
+      for (int j = 0; j < nkv; ++j) {
+        const int sv = j % C::NSTV;
         if (j >= C::NSTV &&
             !mbar_wait(bar(B_VEMPTY + sv), (uint32_t)(j / C::NSTV - 1) & 1u, wc))
           break;
+        loaded = j + 1;
         // test hook (fa_sm100_set_debug_flags bit 0): never load the first V tile,
         // so the PV issuer's wait for it runs out
         if ((debug_flags & 1) && j == 0) continue;
@@ -182,17 +199,12 @@ __global__ void __launch_bounds__(608, 1)
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_V + sv * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
                       bar(B_VFULL + sv), a * C::AE, j * C::BN, h, b);
-        v_last[sv] = j;
       }
-      // After an abort, let the loads this CTA issued land before it exits.
       if (*abort_flag) {
-        mbar_wait_drain(bar(B_QFULL), 0, timeout_ns);
-        for (int s = 0; s < C::NSTK; ++s)
-          if (k_last[s] >= 0)
-            mbar_wait_drain(bar(B_KFULL + s), (uint32_t)(k_last[s] / C::NSTK) & 1u, timeout_ns);
-        for (int s = 0; s < C::NSTV; ++s)
-          if (v_last[s] >= 0)
-            mbar_wait_drain(bar(B_VFULL + s), (uint32_t)(v_last[s] / C::NSTV) & 1u, timeout_ns);
+        for (int j = max(0, loaded - C::NSTV); j < loaded; ++j) {
+          if ((debug_flags & 1) && j == 0) continue;
+          mbar_wait_drain(bar(B_VFULL + j % C::NSTV), (uint32_t)(j / C::NSTV) & 1u, timeout_ns);
+        }
       }
     }
   } else if (warp == 17) {

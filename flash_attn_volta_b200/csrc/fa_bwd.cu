@@ -266,10 +266,11 @@ __global__ void __launch_bounds__(544, 1)
     }
   } else if (warp >= 13) {
     // ------------------------------------------------------------ MMA issuers (warps 13..16)
-    // Each independent MMA chain has its own issuing thread: one thread can have
-    // only about one tcgen05.mma in setup at a time (~90 clk each), so a single
-    // issuer leaves the tensor core idle on these small tiles, while four
-    // concurrent issuers keep it busy.  Roles:
+    // Each independent MMA chain has its own issuing thread: one thread issues
+    // about one tcgen05.mma per ~55 clk, while an M128 x N64 x K16 MMA takes 48
+    // clk with both operands in shared memory (operand reads at 128 B/clk) and 32
+    // with A in tensor memory, so a single issuer would leave the tensor core
+    // idle on these small tiles; four concurrent issuers keep work queued.  Roles:
     //   0: S^T = K Q^T        1: dP^T = V dO^T      (tile i, once the softmax
     //                                                warps hold tile i-1's values)
     //   2: dV += P^T dO, dK += dS^T Q (A operands in TMEM)

@@ -306,6 +306,16 @@ def run_ours(args, wl):
             e1.record(stream)
         torch.cuda.synchronize(dev)
         k_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+
+        def time_phase(p):
+            for e0, e1 in ev:
+                e0.record(stream)
+                phase(p)
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+
+        pre_ms, post_ms = time_phase(0), time_phase(2)
         # forward kernel alone, same method
         evf = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(reps)]
@@ -354,7 +364,8 @@ def run_ours(args, wl):
                          "peak_kind": f"{peak_kind} bf16 burst",
                          "flops_per_launch": bwd_alg, "mean_ms": k_ms,
                          "fwd_kernel": {"achieved": f_tflops, "mean_ms": f_ms,
-                                        "frac": f_tflops / peak_burst}},
+                                        "frac": f_tflops / peak_burst},
+                         "bwd_pre_ms": pre_ms, "bwd_post_ms": post_ms},
             "clocks": clock_info,
         }
         if headline:

@@ -88,6 +88,46 @@ def status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+def status_ptr(idx: int) -> int:
+    """Device address of the status word of CUDA device `idx`."""
+    t = _status.get(idx)
+    if t is None:
+        t = status_word(torch.device("cuda", idx))
+    return t.data_ptr()
+
+
+def stream_ptr(idx: int) -> int:
+    """cudaStream_t of the current torch stream on CUDA device `idx`."""
+    return _raw_stream(idx)
+
+
+def _raw_stream_fallback(idx: int) -> int:
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or _raw_stream_fallback
+
+
+class on_device:
+    """Make CUDA device `idx` current for the block (a no-op when it already is)."""
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, idx: int):
+        self.idx = idx
+        self.prev = -1
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev >= 0:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
 def check_status(device: torch.device | None = None) -> None:
     """Synchronise and raise RuntimeError if a kernel on `device` reported an error."""
     devs = [device] if device is not None else [torch.device("cuda", i) for i in _status]
@@ -100,5 +140,10 @@ def check_status(device: torch.device | None = None) -> None:
                                "(1 = an on-device wait timed out)")
 
 
+_debug_sync = os.environ.get("FA_B200_SYNC_CHECK", "0") == "1"
+
+
 def debug_sync() -> bool:
-    return os.environ.get("FA_B200_SYNC_CHECK", "0") == "1"
+    """FA_B200_SYNC_CHECK=1 (read at import): synchronise and check the status
+    word after every call."""
+    return _debug_sync

@@ -13,7 +13,7 @@ import math
 import torch
 
 from . import _lib
-from .forward import _as_kernel_input, _stream_ptr
+from .forward import _as_kernel_input
 
 
 def flash_attn_backward(
@@ -56,16 +56,17 @@ def flash_attn_backward(
     if q.numel() == 0:
         return dq, dk, dv
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    idx = q.device.index
+    with _lib.on_device(idx):
         nbytes = lib.fa_sm100_bwd_workspace_bytes(B, N, H, D)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-        status = _lib.status_word(q.device)
         rc = lib.fa_sm100_bwd(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                               o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
                               dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, D,
-                              float(sm_scale), 1 if causal else 0, status.data_ptr(),
-                              _stream_ptr(q.device))
-    _lib.check(rc, "fa_sm100_bwd")
+                              float(sm_scale), 1 if causal else 0, _lib.status_ptr(idx),
+                              _lib.stream_ptr(idx))
+    if rc:
+        _lib.check(rc, "fa_sm100_bwd")
     if _lib.debug_sync():
         _lib.check_status(q.device)
     return dq, dk, dv

@@ -44,14 +44,26 @@ EncodeTiledFn encode_fn() {
 // autograd worker, has none, and the driver-level tensor-map encoder then
 // fails with CUDA_ERROR_INVALID_CONTEXT).
 int check_device() {
+  // per host thread: the device whose primary context this thread has bound;
+  // per device: 1 = compute capability 10.0, 2 = not (checked once)
+  thread_local int bound_dev = -1;
+  static std::atomic<int> cc_state[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_DEVICE;
-  if (cudaSetDevice(dev) != cudaSuccess) return FA_ERR_DEVICE;
-  int major = 0, minor = 0;
-  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
-    return FA_ERR_DEVICE;
-  return (major == 10 && minor == 0) ? FA_OK : FA_ERR_DEVICE;
+  if (dev != bound_dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) return FA_ERR_DEVICE;
+    bound_dev = dev;
+  }
+  int state = dev < 64 ? cc_state[dev].load(std::memory_order_relaxed) : 0;
+  if (state == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return FA_ERR_DEVICE;
+    state = (major == 10 && minor == 0) ? 1 : 2;
+    if (dev < 64) cc_state[dev].store(state, std::memory_order_relaxed);
+  }
+  return state == 1 ? FA_OK : FA_ERR_DEVICE;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -109,37 +109,45 @@ enum BwdBar {
 };
 
 // -------------------------------------------------------------------------- pre
-// One warp per (bh, row) of the padded row range.
-__global__ void fa_bwd_pre_kernel(const __half* __restrict__ o, const __half* __restrict__ dout,
-                                  const float* __restrict__ lse, float* __restrict__ lse2,
-                                  float* __restrict__ delta, float* __restrict__ dq_acc, int S,
-                                  int H, int D, int S_pad) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+// D/8 threads per (bh, row) of the padded row range, 16-byte loads of O and dO:
+// delta = rowsum(O * dO), lse2 = LSE * log2(e), and the row of the fp32 dQ
+// accumulator zeroed.
+__global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
+    const __half* __restrict__ o, const __half* __restrict__ dout, const float* __restrict__ lse,
+    float* __restrict__ lse2, float* __restrict__ delta, float* __restrict__ dq_acc, int S, int H,
+    int D, int S_pad) {
+  const int tpr = D / 8;  // threads per row: 2, 4, 8 or 16 (a power of two inside a warp)
+  const int sub = threadIdx.x % tpr;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / tpr;
   const int bh = blockIdx.y;
-  if (row >= S_pad) return;
+  const bool in_pad = row < S_pad;  // always true for the exact grid; kept for the shuffle
   const int b = bh / H, h = bh % H;
   const size_t prow = (size_t)bh * S_pad + row;
   float acc = 0.f;
   if (row < S) {
-    const __half* orow = o + (((size_t)b * S + row) * H + h) * D;
-    const __half* drow = dout + (((size_t)b * S + row) * H + h) * D;
-    for (int e = lane * 2; e < D; e += 64) {
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(orow + e));
-      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(drow + e));
+    const size_t off = (((size_t)b * S + row) * H + h) * D + sub * 8;
+    const uint4 ov = *reinterpret_cast<const uint4*>(o + off);
+    const uint4 dv = *reinterpret_cast<const uint4*>(dout + off);
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&ow[i]));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&dw[i]));
       acc = fmaf(a.x, c.x, acc);
       acc = fmaf(a.y, c.y, acc);
     }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
+  for (int m = tpr / 2; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  if (!in_pad) return;
+  if (sub == 0) {
     delta[prow] = acc;
     lse2[prow] = row < S ? lse[(size_t)bh * S + row] * 1.4426950408889634f
                          : __int_as_float(0x7f800000);
   }
-  float* qa = dq_acc + prow * D;
-  for (int e = lane * 4; e < D; e += 128) *reinterpret_cast<float4*>(qa + e) = make_float4(0, 0, 0, 0);
+  float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
+  qa[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  qa[1] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // -------------------------------------------------------------------------- post
@@ -573,8 +581,7 @@ __global__ void __launch_bounds__(544, 1)
 template <int D>
 static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   using C = BwdCfg<D>;
-  if (cudaFuncSetAttribute(fa_bwd_main_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           C::SMEM) != cudaSuccess)
+  if (!smem_attr_set<1000 + D>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.H * ((a.S + C::BN - 1) / C::BN));
   fa_bwd_main_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
@@ -588,7 +595,8 @@ int bwd_q_rows(int D) { return D == 128 ? 64 : 128; }
 
 int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
   if (phase < 0 || phase == 0) {
-    dim3 grid((a.S_pad + 7) / 8, a.B * a.H);
+    const int rows_per_block = 256 / (a.D / 8);
+    dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
     fa_bwd_pre_kernel<<<grid, 256, 0, stream>>>(
         static_cast<const __half*>(a.o), static_cast<const __half*>(a.dout), a.lse, a.lse2,
         a.delta, a.dq_acc, a.S, a.H, a.D, a.S_pad);

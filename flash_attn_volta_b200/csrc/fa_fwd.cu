@@ -440,8 +440,7 @@ __global__ void __launch_bounds__(640, 1)
 template <int D>
 static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<D>;
-  if (cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           C::SMEM) != cudaSuccess)
+  if (!smem_attr_set<D>(reinterpret_cast<const void*>(fa_fwd_kernel<D>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
   fa_fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(

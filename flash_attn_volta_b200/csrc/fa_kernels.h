@@ -3,6 +3,8 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 
@@ -44,6 +46,22 @@ struct BwdArgs {
   int* status;
   unsigned long long timeout_ns;
 };
+
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute
+// is per device and function; setting it on every launch costs a driver call).
+// `Tag` separates the callers' kernels; devices beyond 64 are set every time.
+template <int Tag>
+inline bool smem_attr_set(const void* func, int bytes) {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return true;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 // phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion

@@ -26,7 +26,8 @@ def _as_kernel_input(t: torch.Tensor) -> torch.Tensor:
 
 
 def _stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return _lib.stream_ptr(idx)
 
 
 def flash_attn_forward(
@@ -64,13 +65,14 @@ def flash_attn_forward(
     lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if return_softmax_lse else None
     if q.numel() != 0:
         lib = _lib.load()
-        with torch.cuda.device(q.device):
-            status = _lib.status_word(q.device)
+        idx = q.device.index
+        with _lib.on_device(idx):
             rc = lib.fa_sm100_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                   lse.data_ptr() if lse is not None else None,
                                   B, N, H, D, float(sm_scale), 1 if causal else 0,
-                                  status.data_ptr(), _stream_ptr(q.device))
-        _lib.check(rc, "fa_sm100_fwd")
+                                  _lib.status_ptr(idx), _lib.stream_ptr(idx))
+        if rc:
+            _lib.check(rc, "fa_sm100_fwd")
         if _lib.debug_sync():
             _lib.check_status(q.device)
     if return_softmax_lse:

@@ -47,9 +47,18 @@ __device__ unsigned long long g_trace[64][16];
   do {                                                                               \
     if (blockIdx.x == 0 && (it) < 64) g_trace[it][slot] = clock64(); \
   } while (0)
+// per-CTA timeline: SM id, globaltimer at entry, at the first S issue, at exit
+__device__ unsigned long long g_bcta[8192][4];
+#define CTRACE(slot)                                                                 \
+  do {                                                                               \
+    if (blockIdx.x < 8192) g_bcta[blockIdx.x][slot] = globaltimer_ns();             \
+  } while (0)
 #else
 #define TRACE(slot, it) \
   do {                  \
+  } while (0)
+#define CTRACE(slot) \
+  do {               \
   } while (0)
 #endif
 
@@ -116,6 +125,8 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const __half* __restrict__ o, const __half* __restrict__ dout, const float* __restrict__ lse,
     float* __restrict__ lse2, float* __restrict__ delta, float* __restrict__ dq_acc, int S, int H,
     int D, int S_pad) {
+  griddep_wait();  // O and LSE come from the forward
+  griddep_launch_dependents();
   const int tpr = D / 8;  // threads per row: 2, 4, 8 or 16 (a power of two inside a warp)
   const int sub = threadIdx.x % tpr;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) / tpr;
@@ -154,6 +165,8 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
 __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __restrict__ dq, int S,
                                    int H, int D, int S_pad, float scale) {
   // one thread per 8 consecutive elements of one (b, s, h) row
+  griddep_wait();  // the dQ accumulator comes from the main kernel
+  griddep_launch_dependents();
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = D / 8;
   const size_t rows = (size_t)gridDim.y * S;
@@ -197,6 +210,14 @@ __global__ void __launch_bounds__(544, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * C_COUNT + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    CTRACE(1);
+#ifdef FA_BWD_TRACE
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    if (blockIdx.x < 8192) g_bcta[blockIdx.x][0] = smid;
+#endif
+  }
   // 1-D grid over (head group, key block, head): key block 0 (the most query
   // tiles under a causal mask) first inside each group of heads
   const int nkt = (S + C::BN - 1) / C::BN;
@@ -229,6 +250,13 @@ __global__ void __launch_bounds__(544, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Set-up overlaps the previous kernel (the prep kernel, whose LSE2 / delta /
+  // zeroed dQ accumulator this kernel uses); K and V, written before it, are
+  // loaded before the wait.
+  if (warp != 12) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
 
   if (warp == 12) {
     // ------------------------------------------------------------ TMA producer
@@ -242,6 +270,10 @@ __global__ void __launch_bounds__(544, 1)
         tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, h, b);
         tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, h, b);
       }
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    if (lane == 0) {
       int q_last[C::NST];  // last query tile loaded into each stage
       for (int t = 0; t < C::NST; ++t) q_last[t] = -1;
       for (int i = 0; i < nq; ++i) {
@@ -304,6 +336,7 @@ __global__ void __launch_bounds__(544, 1)
               (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)))
             break;
           if (role == 0) TRACE(2, i);
+          if (role == 0 && i == 0) CTRACE(2);
           tc_fence_after();
           const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
           const uint32_t bbase = role == 0 ? qb : dob;
@@ -575,6 +608,7 @@ __global__ void __launch_bounds__(544, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+    if (lane == 0) CTRACE(3);
   }
 }
 
@@ -584,11 +618,11 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   if (!smem_attr_set<1000 + D>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.H * ((a.S + C::BN - 1) / C::BN));
-  fa_bwd_main_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
-      *a.tm_q, *a.tm_do, *a.tm_k, *a.tm_v, a.lse2, a.delta, a.dq_acc, static_cast<__half*>(a.dk),
-      static_cast<__half*>(a.dv), a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f,
-      a.causal, a.status, a.timeout_ns);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  const cudaError_t e = launch_pdl(
+      fa_bwd_main_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do, *a.tm_k,
+      *a.tm_v, a.lse2, a.delta, a.dq_acc, static_cast<__half*>(a.dk), static_cast<__half*>(a.dv),
+      a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns);
+  return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 int bwd_q_rows(int D) { return D == 128 ? 64 : 128; }
@@ -597,10 +631,10 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
   if (phase < 0 || phase == 0) {
     const int rows_per_block = 256 / (a.D / 8);
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
-    fa_bwd_pre_kernel<<<grid, 256, 0, stream>>>(
-        static_cast<const __half*>(a.o), static_cast<const __half*>(a.dout), a.lse, a.lse2,
-        a.delta, a.dq_acc, a.S, a.H, a.D, a.S_pad);
-    if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+    if (launch_pdl(fa_bwd_pre_kernel, grid, dim3(256), 0, stream, static_cast<const __half*>(a.o),
+                   static_cast<const __half*>(a.dout), a.lse, a.lse2, a.delta, a.dq_acc, a.S, a.H,
+                   a.D, a.S_pad) != cudaSuccess)
+      return FA_ERR_LAUNCH;
   }
   int rc = FA_OK;
   if (phase < 0 || phase == 1) switch (a.D) {
@@ -615,9 +649,9 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
     const int per_row = a.D / 8;
     const size_t n = (size_t)a.S * per_row;
     dim3 grid((unsigned)((n + 255) / 256), a.B * a.H);
-    fa_bwd_post_kernel<<<grid, 256, 0, stream>>>(a.dq_acc, static_cast<__half*>(a.dq), a.S, a.H,
-                                                 a.D, a.S_pad, a.scale);
-    if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+    if (launch_pdl(fa_bwd_post_kernel, grid, dim3(256), 0, stream, a.dq_acc,
+                   static_cast<__half*>(a.dq), a.S, a.H, a.D, a.S_pad, a.scale) != cudaSuccess)
+      return FA_ERR_LAUNCH;
   }
   return FA_OK;
 }
@@ -627,5 +661,8 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
 #ifdef FA_BWD_TRACE
 extern "C" int fa_debug_trace(void* dst) {
   return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_trace, sizeof(fa_sm100::g_trace));
+}
+extern "C" int fa_debug_trace_bwd_cta(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_bcta, sizeof(fa_sm100::g_bcta));
 }
 #endif

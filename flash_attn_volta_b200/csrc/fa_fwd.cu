@@ -54,9 +54,18 @@ __device__ unsigned long long g_ftrace[64][16];
   do {                                                                                      \
     if (blockIdx.x == FA_TRACE_BLOCK && (it) < 64) g_ftrace[it][slot] = clock64();           \
   } while (0)
+// per-CTA timeline: SM id, globaltimer at entry, at the first S issue, at exit
+__device__ unsigned long long g_fcta[8192][4];
+#define CTRACE(slot)                                                                        \
+  do {                                                                                      \
+    if (blockIdx.x < 8192) g_fcta[blockIdx.x][slot] = globaltimer_ns();                     \
+  } while (0)
 #else
 #define FTRACE(slot, it) \
   do {                   \
+  } while (0)
+#define CTRACE(slot) \
+  do {               \
   } while (0)
 #endif
 
@@ -118,6 +127,14 @@ __global__ void __launch_bounds__(640, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * B_COUNT + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    CTRACE(1);
+#ifdef FA_FWD_TRACE
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    if (blockIdx.x < 8192) g_fcta[blockIdx.x][0] = smid;
+#endif
+  }
   // 1-D grid over (head group, query block rank, head): longest blocks first
   // inside each group of heads, K/V of only a few heads live at once (L2 reuse)
   const int nblk = (S + C::BM - 1) / C::BM;
@@ -150,6 +167,9 @@ __global__ void __launch_bounds__(640, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Set-up above overlaps the previous kernel's tail; inputs are read below.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 16) {
     // ------------------------------------------------------------ TMA producer: Q, K
@@ -220,6 +240,7 @@ __global__ void __launch_bounds__(640, 1)
             (j >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)))
           break;
         FTRACE(0, j);
+        if (j == 0) CTRACE(2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -434,6 +455,7 @@ __global__ void __launch_bounds__(640, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+    if (lane == 0) CTRACE(3);
   }
 }
 
@@ -443,10 +465,11 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   if (!smem_attr_set<D>(reinterpret_cast<const void*>(fa_fwd_kernel<D>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
-  fa_fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse, a.S, a.H,
-      a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns, a.debug_flags);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  const cudaError_t e = launch_pdl(fa_fwd_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream,
+                                   *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse,
+                                   a.S, a.H, a.scale * 1.4426950408889634f, a.causal, a.status,
+                                   a.timeout_ns, a.debug_flags);
+  return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
@@ -464,5 +487,8 @@ int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
 #ifdef FA_FWD_TRACE
 extern "C" int fa_debug_trace_fwd(void* dst) {
   return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_ftrace, sizeof(fa_sm100::g_ftrace));
+}
+extern "C" int fa_debug_trace_fwd_cta(void* dst) {
+  return (int)cudaMemcpyFromSymbol(dst, fa_sm100::g_fcta, sizeof(fa_sm100::g_fcta));
 }
 #endif

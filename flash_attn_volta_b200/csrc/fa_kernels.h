@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 #include "../../include/fa_sm100.h"
 
@@ -61,6 +62,25 @@ inline bool smem_attr_set(const void* func, int bytes) {
     return false;
   done.fetch_or(bit, std::memory_order_acq_rel);
   return true;
+}
+
+// Launch with programmatic stream serialization: the kernel may start while the
+// previous kernel in the stream finishes (it calls griddep_wait() before reading
+// that kernel's outputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);

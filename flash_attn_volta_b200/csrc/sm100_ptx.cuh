@@ -107,6 +107,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
   return mbar_wait_slow(bar, parity, w);
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch.  A grid launched with programmatic stream
+// serialization may start while the previous grid in the stream runs;
+// griddep_wait() returns once that grid has completed and its memory is visible
+// (at once for a normal launch).  griddep_launch_dependents() lets the next such
+// grid start; every kernel here calls it only after its own griddep_wait(), so
+// when a grid starts early, everything before its predecessor has completed.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -106,7 +106,7 @@ int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, i
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WsLayout {
-  size_t dq_acc, lse2, delta, total;
+  size_t dq_acc, q_aug, do_aug, total;
 };
 
 WsLayout ws_layout(int B, int S, int H, int D) {
@@ -114,9 +114,9 @@ WsLayout ws_layout(int B, int S, int H, int D) {
   const size_t rows = (size_t)B * H * S_pad;
   WsLayout w;
   w.dq_acc = 0;
-  w.lse2 = round_up(rows * D * sizeof(float), 256);
-  w.delta = w.lse2 + round_up(rows * sizeof(float), 256);
-  w.total = w.delta + round_up(rows * sizeof(float), 256);
+  w.q_aug = round_up(rows * D * sizeof(float), 256);
+  w.do_aug = w.q_aug + round_up(rows * kAugRowBytes, 256);
+  w.total = w.do_aug + round_up(rows * kAugRowBytes, 256);
   return w;
 }
 
@@ -219,8 +219,8 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   a.dk = dk;
   a.dv = dv;
   a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
-  a.lse2 = reinterpret_cast<float*>(ws + w.lse2);
-  a.delta = reinterpret_cast<float*>(ws + w.delta);
+  a.q_aug = ws + w.q_aug;
+  a.do_aug = ws + w.do_aug;
   a.B = batch;
   a.S = seqlen;
   a.H = nheads;

@@ -9,22 +9,32 @@
 // over key blocks) with 7 GEMMs; here one kernel per key block computes all
 // five GEMMs and accumulates dQ into an fp32 workspace with L2 reductions.
 //
+// The row terms LSE and delta ride in the MMAs: Q and dO get one extra K step
+// of 16 columns holding -LSE/scale (resp. -delta) as an fp16 hi/lo pair, K and
+// V the matching step [1, 1, 0, ...], so the tensor core delivers
+// S'^T = S^T - LSE/scale and dP'^T = dP^T - delta and the softmax warps read no
+// per-column values from shared memory (a value broadcast to all lanes costs
+// four shared-memory wavefronts per 128-bit load, which competes with the
+// tensor core's operand reads).  The hi/lo pair keeps the term exact to ~1e-5.
+//
 // Kernels:
-//   fa_bwd_pre   delta (fp32), LSE * log2(e), zero the dQ accumulator.
+//   fa_bwd_pre   delta = rowsum(O * dO), the extra K-step rows of Q and dO in the
+//                MMA's no-swizzle K-major layout, zero the dQ accumulator.
 //   fa_bwd_main  one CTA = one 128-row key/value tile of one (batch, head);
 //                loops over query tiles of BM rows (64 for D=128, else 128).
 //     warps 0-7  "softmax": warp w owns key rows 32*(w%4).. (its TMEM lane
 //                quarter) and half of the query columns.  Loads S^T and dP^T
 //                from tensor memory into registers and releases them at once
 //                (so the next tile's S^T / dP^T MMAs run while it computes),
-//                P^T = exp2(S^T*scale*log2e - LSE2), dS^T = P^T (dP^T - delta);
+//                P^T = exp2(S'^T * scale * log2e), dS^T = P^T dP'^T;
 //                P^T (fp16) goes to tensor memory as the A operand of dV += P^T dO,
 //                dS^T to shared memory (for dQ) and, for D=128, to tensor memory
 //                too (A operand of dK += dS^T Q); final dK/dV epilogue.
 //     warps 8-11 dQ epilogue: read this tile's dQ partial from tensor memory,
 //                stage it in shared memory and add it into the fp32 accumulator
 //                with one bulk reduction (cp.reduce.async.bulk .add.f32).
-//     warp 12    TMA producer (K, V once; Q, dO, LSE2, delta per query tile).
+//     warp 12    TMA producer (K, V once; Q, dO and their extra K-step rows per
+//                query tile).
 //     warps 13-16 MMA issuers, one per independent chain: S^T = K Q^T,
 //                dP^T = V dO^T (issued as soon as the previous tile's values are
 //                in registers), dV += P^T dO with dK += dS^T Q, and the dQ
@@ -70,7 +80,7 @@ struct BwdCfg {
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;
   static constexpr int AE = SWB / 2;
   static constexpr int NAT = D / AE;
-  static constexpr int NST = 3;  // Q / dO / LSE2 / delta ring depth
+  static constexpr int NST = 3;  // Q / dO (+ their extra K-step rows) ring depth
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int PT_BYTES = BN * BM * 2;  // [key row][query col], 64-col atoms
@@ -78,9 +88,14 @@ struct BwdCfg {
   static constexpr int OFF_V = OFF_K + KV_BYTES;
   static constexpr int OFF_Q = OFF_V + KV_BYTES;
   static constexpr int OFF_DO = OFF_Q + NST * Q_BYTES;
-  static constexpr int OFF_LSE = OFF_DO + NST * Q_BYTES;
-  static constexpr int OFF_DELTA = OFF_LSE + NST * BM * 4;
-  static constexpr int OFF_BAR = OFF_DELTA + NST * BM * 4;  // barriers, TMEM slot, abort flag
+  // extra K step (16 columns, no-swizzle K-major: 8-row core matrices of 16 B,
+  // the two 8-column halves 128 B apart, row groups 256 B apart): the [1, 1, 0,
+  // ...] rows shared by K and V, and per stage the rows of Q and of dO
+  static constexpr int AUG_BYTES = BM * kAugRowBytes;
+  static constexpr int OFF_ONE = OFF_DO + NST * Q_BYTES;
+  static constexpr int OFF_QA = OFF_ONE + BN * kAugRowBytes;
+  static constexpr int OFF_DA = OFF_QA + NST * AUG_BYTES;
+  static constexpr int OFF_BAR = OFF_DA + NST * AUG_BYTES;  // barriers, TMEM slot, abort flag
   static constexpr int OFF_P = ((OFF_BAR + 256) + 1023) / 1024 * 1024;
   static constexpr int OFF_DS = OFF_P;  // P^T lives in tensor memory, not here
   static constexpr int DQ_STAGE_BYTES = BM * D * 4;  // one dQ partial, [q][d] fp32
@@ -118,13 +133,31 @@ enum BwdBar {
 };
 
 // -------------------------------------------------------------------------- pre
+// Byte offset of element k of `row` in the extra K-step tile of a row block
+// (no-swizzle K-major: row group of 8 at 256 B, the two 8-column halves 128 B
+// apart, rows 16 B apart inside a core matrix).
+__host__ __device__ constexpr uint32_t aug_offset(uint32_t row, uint32_t k) {
+  return (row / 8) * 256 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2;
+}
+
+// x as an fp16 pair with hi + lo == x to ~2^-22 |x| (hi clamped to the fp16
+// range; a non-finite x, i.e. a fully masked row, becomes a large negative
+// term that drives every P of the row to zero).
+__device__ __forceinline__ uint32_t split_half2(float x) {
+  if (!(fabsf(x) <= 60000.f)) x = (x > 0.f) ? 60000.f : -60000.f;
+  const __half hi = __float2half_rn(x);
+  const __half lo = __float2half_rn(x - __half2float(hi));
+  return (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+}
+
 // D/8 threads per (bh, row) of the padded row range, 16-byte loads of O and dO:
-// delta = rowsum(O * dO), lse2 = LSE * log2(e), and the row of the fp32 dQ
-// accumulator zeroed.
+// delta = rowsum(O * dO); the row's extra K-step entries [hi, lo, 0, ...] of
+// -LSE/scale (Q side) and -delta (dO side); the row of the fp32 dQ accumulator
+// zeroed.
 __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const __half* __restrict__ o, const __half* __restrict__ dout, const float* __restrict__ lse,
-    float* __restrict__ lse2, float* __restrict__ delta, float* __restrict__ dq_acc, int S, int H,
-    int D, int S_pad) {
+    uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc, int S,
+    int H, int D, int S_pad, float inv_scale) {
   griddep_wait();  // O and LSE come from the forward
   griddep_launch_dependents();
   const int tpr = D / 8;  // threads per row: 2, 4, 8 or 16 (a power of two inside a warp)
@@ -152,9 +185,16 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
   for (int m = tpr / 2; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
   if (!in_pad) return;
   if (sub == 0) {
-    delta[prow] = acc;
-    lse2[prow] = row < S ? lse[(size_t)bh * S + row] * 1.4426950408889634f
-                         : __int_as_float(0x7f800000);
+    const float l = row < S ? lse[(size_t)bh * S + row] : __int_as_float(0x7f800000);
+    // row blocks of S_pad rows per (batch, head); S_pad is a multiple of 8
+    const size_t base = (size_t)bh * S_pad * kAugRowBytes;
+    const uint32_t r = (uint32_t)row;
+    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 0)) =
+        make_uint4(split_half2(-l * inv_scale), 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) =
+        make_uint4(split_half2(-acc), 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
   }
   float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
   qa[0] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -193,8 +233,9 @@ __global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ lse2,
-                       const float* __restrict__ delta, float* __restrict__ dq_acc,
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
+                       float* __restrict__ dq_acc,
                        __half* __restrict__ dk, __half* __restrict__ dv, int S, int H, int S_pad,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
@@ -246,13 +287,20 @@ __global__ void __launch_bounds__(544, 1)
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
+  if (warp >= 8 && warp < 12) {
+    // the extra K-step rows of K and V: [1, 1, 0, ...] for each of the 128 key rows
+    const uint32_t r = threadIdx.x - 256;
+    st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 0), 0x3C003C00u, 0u, 0u, 0u);
+    st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 8), 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Set-up overlaps the previous kernel (the prep kernel, whose LSE2 / delta /
-  // zeroed dQ accumulator this kernel uses); K and V, written before it, are
-  // loaded before the wait.
+  // Set-up overlaps the previous kernel (the prep kernel, whose extra K-step
+  // rows and zeroed dQ accumulator this kernel uses); K and V, written before
+  // it, are loaded before the wait.
   if (warp != 12) {
     griddep_wait();
     griddep_launch_dependents();
@@ -283,17 +331,18 @@ __global__ void __launch_bounds__(544, 1)
         TRACE(0, i);
         if (i >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
         TRACE(1, i);
-        mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::BM * 4);
+        mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::AUG_BYTES);
         for (int a = 0; a < C::NAT; ++a) {
           tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
                       bar(C_QFULL + st), a * C::AE, q0, h, b);
           tma_load_4d(sbase + C::OFF_DO + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_do,
                       bar(C_QFULL + st), a * C::AE, q0, h, b);
         }
-        bulk_load(sbase + C::OFF_LSE + st * C::BM * 4, lse2 + (size_t)bh * S_pad + q0, C::BM * 4,
+        const size_t aug = ((size_t)bh * S_pad + q0) * kAugRowBytes;
+        bulk_load(sbase + C::OFF_QA + st * C::AUG_BYTES, q_aug + aug, C::AUG_BYTES,
                   bar(C_QFULL + st));
-        bulk_load(sbase + C::OFF_DELTA + st * C::BM * 4, delta + (size_t)bh * S_pad + q0,
-                  C::BM * 4, bar(C_QFULL + st));
+        bulk_load(sbase + C::OFF_DA + st * C::AUG_BYTES, do_aug + aug, C::AUG_BYTES,
+                  bar(C_QFULL + st));
         q_last[st] = i;
       }
       // After an abort, let the loads this CTA issued land before it exits.
@@ -349,6 +398,11 @@ __global__ void __launch_bounds__(544, 1)
             const uint64_t bd = make_smem_desc(bbase + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
             mma_f16_ss(dcol, ad, bd, id_s, kk > 0 ? 1u : 0u);
           }
+          // extra K step: + (-LSE/scale) resp. + (-delta) for each query column
+          mma_f16_ss(dcol, make_smem_desc(sbase + C::OFF_ONE, 128, 256, 0),
+                     make_smem_desc(sbase + (role == 0 ? C::OFF_QA : C::OFF_DA) + st * C::AUG_BYTES,
+                                    128, 256, 0),
+                     id_s, 1u);
           mma_commit(bar(C_SFULL));
           if (role == 0) TRACE(3, i);
         } else if (role == 2) {
@@ -423,8 +477,6 @@ __global__ void __launch_bounds__(544, 1)
       }
       if (threadIdx.x == 0) TRACE(7, i);
       tc_fence_after();
-      const float* lse_s = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * C::BM * 4);
-      const float* del_s = reinterpret_cast<const float*>(smem + C::OFF_DELTA + st * C::BM * 4);
       // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
       // dP^T are released after the last chunk's loads; P^T / dS^T are written only
       // once the previous tile's dV / dK MMAs have read them (PFREE).
@@ -441,22 +493,19 @@ __global__ void __launch_bounds__(544, 1)
           if (lane == 0) mbar_arrive(bar(C_SFREE));
           if (threadIdx.x == 0) TRACE(8, i);
         }
-        // P^T and dS^T for these 32 query columns, packed to fp16 pairs
+        // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
+        // dP'^T already hold -LSE/scale and -delta)
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(lse_s + cb + e);
-          const float4 d4 = *reinterpret_cast<const float4*>(del_s + cb + e);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dv4[4] = {d4.x, d4.y, d4.z, d4.w};
           float p4[4], ds4[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int ql = cb + e + u;
             const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
-            const float pe = valid ? ex2(fmaf(__uint_as_float(sr[e + u]), scale_log2, -lv[u])) : 0.f;
+            const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
             p4[u] = pe;
-            ds4[u] = pe * (__uint_as_float(dr[e + u]) - dv4[u]);
+            ds4[u] = pe * __uint_as_float(dr[e + u]);
           }
           pp[e / 2] = pack_half2(p4[0], p4[1]);
           pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
@@ -620,7 +669,7 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   dim3 grid(a.B * a.H * ((a.S + C::BN - 1) / C::BN));
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do, *a.tm_k,
-      *a.tm_v, a.lse2, a.delta, a.dq_acc, static_cast<__half*>(a.dk), static_cast<__half*>(a.dv),
+      *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<__half*>(a.dk), static_cast<__half*>(a.dv),
       a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
@@ -632,8 +681,8 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
     const int rows_per_block = 256 / (a.D / 8);
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
     if (launch_pdl(fa_bwd_pre_kernel, grid, dim3(256), 0, stream, static_cast<const __half*>(a.o),
-                   static_cast<const __half*>(a.dout), a.lse, a.lse2, a.delta, a.dq_acc, a.S, a.H,
-                   a.D, a.S_pad) != cudaSuccess)
+                   static_cast<const __half*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.S,
+                   a.H, a.D, a.S_pad, 1.0f / a.scale) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   int rc = FA_OK;

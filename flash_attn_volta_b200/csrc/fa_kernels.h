@@ -39,8 +39,10 @@ struct BwdArgs {
   void* dk;
   void* dv;
   float* dq_acc;   // (B*H, S_pad, D) fp32
-  float* lse2;     // (B*H, S_pad) fp32, lse * log2(e), +inf in padding rows
-  float* delta;    // (B*H, S_pad) fp32
+  // (B*H, S_pad) rows of 16 fp16 in the MMA's no-swizzle K-major layout: the
+  // extra K step of S^T (-LSE/scale) and of dP^T (-delta) as fp16 hi/lo pairs
+  uint8_t* q_aug;
+  uint8_t* do_aug;
   int B, S, H, D, S_pad;
   float scale;
   int causal;
@@ -82,6 +84,9 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// Bytes of one row of the augmented K step (16 fp16).
+constexpr int kAugRowBytes = 32;
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 // phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion

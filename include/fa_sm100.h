@@ -44,7 +44,8 @@ int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* 
                  int* status, void* stream);
 
 /* Bytes of device workspace fa_sm100_bwd needs for this shape (fp32 dQ
- * accumulator, per-row delta and log2-scaled LSE, rows padded to 128). */
+ * accumulator and 32 bytes per row each for the -LSE/scale and -delta terms
+ * the main kernel adds inside its MMAs, rows padded to 128). */
 size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim);
 
 /* Backward: given dout, the forward inputs q, k, v, its output `out` and LSE,
@@ -59,7 +60,7 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  float sm_scale, int causal, int* status, void* stream);
 
 /* The three launches fa_sm100_bwd makes, one at a time, on the same arguments:
- * phase 0 = delta / log2-LSE preparation and zeroing of the dQ accumulator,
+ * phase 0 = delta and the -LSE/scale, -delta MMA terms, zeroing of the dQ accumulator,
  * phase 1 = the main backward kernel (dK, dV, dQ partial sums),
  * phase 2 = dQ accumulator -> fp16 dq.  Running 0, 1, 2 in stream order equals
  * one fa_sm100_bwd call.  For callers that schedule or time the phases apart.

@@ -97,15 +97,53 @@ def gen_shard(B0, B1, S, H, D, amp, device, seed_base=1234):
 
 # ----------------------------------------------------------------------- clocks
 class ClockSampler:
+    """SM clock and clock-event reasons sampled during a timed region.
+
+    NVML read by a background thread every 5 ms (the GPU matched to the CUDA
+    device by UUID), else `nvidia-smi -lms 50`.  Only reads; changes nothing."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index):
         self.gpu_index = gpu_index
         self.proc = None
+        self.thread = None
+        self.samples = []
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.gpu_index).uuid)
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
 
     def start(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.stop_flag = threading.Event()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def loop():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    time.sleep(0.005)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.nv, self.h, self.mx = nv, h, mx
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -115,6 +153,17 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            rows = self.samples
+            if not rows:  # a timed region shorter than the period: one sample now
+                nv, h = self.nv, self.h
+                rows = [(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), self.mx,
+                         nv.nvmlDeviceGetCurrentClocksEventReasons(h))]
+            reasons = sorted({n for _, _, bits in rows for n, m in self.REASONS if bits & m})
+            return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                    "reasons": reasons, "samples": len(rows), "source": "nvml, 5 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -133,7 +182,7 @@ class ClockSampler:
                           and "Not" not in r[5 + i]})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi, 50 ms"}
 
 
 # ----------------------------------------------------------------------- CPU path

@@ -96,11 +96,29 @@ def gen_shard(B0, B1, S, H, D, amp, device, seed_base=1234):
 
 
 # ----------------------------------------------------------------------- clocks
+_NVML_SAMPLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+uuid, idx, period = sys.argv[1], int(sys.argv[2]), float(sys.argv[3])
+try:
+    h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+print("ready", flush=True)
+while True:
+    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    print(sm, mx, bits, flush=True)
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
     """SM clock and clock-event reasons sampled during a timed region.
 
-    NVML read by a background thread every 5 ms (the GPU matched to the CUDA
-    device by UUID), else `nvidia-smi -lms 50`.  Only reads; changes nothing."""
+    A child process reads NVML every 5 ms (the GPU matched to the CUDA device
+    by UUID), else `nvidia-smi -lms 50`.  Only reads; changes nothing."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -110,68 +128,55 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu_index = gpu_index
         self.proc = None
-        self.thread = None
-        self.samples = []
-
-    def _nvml_handle(self):
-        import pynvml
-        pynvml.nvmlInit()
-        uuid = str(torch.cuda.get_device_properties(self.gpu_index).uuid)
-        try:
-            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
-        except Exception:
-            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+        self.kind = None
 
     def start(self):
-        import threading
         try:
-            nv, h = self._nvml_handle()
-            self.stop_flag = threading.Event()
-            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-
-            def loop():
-                while not self.stop_flag.is_set():
-                    try:
-                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
-                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
-                    except Exception:
-                        pass
-                    time.sleep(0.005)
-
-            self.thread = threading.Thread(target=loop, daemon=True)
-            self.nv, self.h, self.mx = nv, h, mx
-            self.thread.start()
-            return
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.gpu_index).uuid)
+            self.proc = subprocess.Popen(
+                [sys.executable, "-c", _NVML_SAMPLER, uuid, str(self.gpu_index), "0.005"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            if self.proc.stdout.readline().strip() == "ready":
+                self.kind = "nvml"
+                return
+            self.proc.kill()
         except Exception:
-            self.thread = None
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50", "-i", str(self.gpu_index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.kind = "nvidia-smi"
         except Exception:
             self.proc = None
 
-    def stop(self):
-        if self.thread is not None:
-            self.stop_flag.set()
-            self.thread.join(timeout=2)
-            rows = self.samples
-            if not rows:  # a timed region shorter than the period: one sample now
-                nv, h = self.nv, self.h
-                rows = [(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), self.mx,
-                         nv.nvmlDeviceGetCurrentClocksEventReasons(h))]
-            reasons = sorted({n for _, _, bits in rows for n, m in self.REASONS if bits & m})
-            return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
-                    "reasons": reasons, "samples": len(rows), "source": "nvml, 5 ms"}
-        if self.proc is None:
-            return None
+    def _collect(self):
+        if self.kind == "nvml":
+            time.sleep(0.01)  # a timed region shorter than the period still gets a sample
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except Exception:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        return out
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        out = self._collect()
+        if self.kind == "nvml":
+            rows = []
+            for line in out.splitlines():
+                f = line.split()
+                if len(f) == 3 and all(x.isdigit() for x in f):
+                    rows.append(tuple(int(x) for x in f))
+            if not rows:
+                return None
+            reasons = sorted({n for _, _, bits in rows for n, m in self.REASONS if bits & m})
+            return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                    "reasons": reasons, "samples": len(rows), "source": "nvml, 5 ms"}
         rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
         if not rows:
             return None

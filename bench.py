@@ -58,7 +58,7 @@ L2_BYTES = 126 * 1000 * 1000
 # DRAM bytes (read + write) per launch of the main backward kernel, from one ncu
 # capture of a 1/16-size case scaled by the (batch, head) count; see
 # profiles/fa_kernels_d128_s8192_full.md.
-BWD_TRAFFIC_PER_LAUNCH = {"c4": 4.76e9}
+BWD_TRAFFIC_PER_LAUNCH = {"c4": 5.04e9}
 
 
 def flops_fwd(B, S, H, D, causal):

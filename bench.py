@@ -55,9 +55,8 @@ WORKLOADS = {
 L2_BYTES = 126 * 1000 * 1000
 
 
-# DRAM bytes (read + write) per launch of the main backward kernel, from one ncu
-# capture of a 1/16-size case scaled by the (batch, head) count; see
-# profiles/fa_kernels_d128_s8192_full.md.
+# DRAM bytes (read + write) per launch of the main backward kernel: one ncu
+# capture of the p8k workload (1/16 of c4's (batch, head) pairs), scaled by 16.
 BWD_TRAFFIC_PER_LAUNCH = {"c4": 5.04e9}
 
 

@@ -1,6 +1,6 @@
 """Ring context-parallel attention over the sequence axis (NCCL send/recv).
 
-For sequences too long for one GPU's time budget (long
+For sequences too long for one GPU's time budget (the long-context training
 variant: B=1, S=131072, H=32, D=128, causal over 8 GPUs).  The reference has
 no multi-GPU path; this is the build's own design on top of the single-GPU
 kernels:

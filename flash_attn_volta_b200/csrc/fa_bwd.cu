@@ -481,12 +481,15 @@ __global__ void __launch_bounds__(544, 1)
       // dP^T are released after the last chunk's loads; P^T / dS^T are written only
       // once the previous tile's dV / dK MMAs have read them (PFREE).
 #pragma unroll 1
+      // every (query, key) pair of this tile is unmasked
+      const bool full_tile = (kv0 + C::BN <= S) && (!causal || q0 >= kv0 + C::BN - 1);
       for (int cc = 0; cc < HW / 32; ++cc) {
         const int cb = c0 + cc * 32;  // first query column of this chunk
         uint32_t sr[32], dr[32];
         tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
         tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
         tmem_wait_ld();
+        if (threadIdx.x == 0 && cc == 0) TRACE(14, i);
         if (cc == HW / 32 - 1) {
           tc_fence_before();
           __syncwarp();
@@ -494,23 +497,41 @@ __global__ void __launch_bounds__(544, 1)
           if (threadIdx.x == 0) TRACE(8, i);
         }
         // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
-        // dP'^T already hold -LSE/scale and -delta)
+        // dP'^T already hold -LSE/scale and -delta).  Only tiles that cross the
+        // causal diagonal or the end of the sequence need the per-element mask.
         uint32_t pp[16], dd[16];
+        if (full_tile) {
+          const uint64_t c2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          float p4[4], ds4[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int ql = cb + e + u;
-            const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
-            const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
-            p4[u] = pe;
-            ds4[u] = pe * __uint_as_float(dr[e + u]);
+          for (int k = 0; k < 16; ++k) {
+            float x0, x1;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2),
+                      x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            float d0, d1;
+            f2_unpack(f2_mul(f2_pack(p0, p1),
+                             f2_pack(__uint_as_float(dr[2 * k]), __uint_as_float(dr[2 * k + 1]))),
+                      d0, d1);
+            pp[k] = pack_half2(p0, p1);
+            dd[k] = pack_half2(d0, d1);
           }
-          pp[e / 2] = pack_half2(p4[0], p4[1]);
-          pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
-          dd[e / 2] = pack_half2(ds4[0], ds4[1]);
-          dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float p4[4], ds4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int ql = cb + e + u;
+              const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
+              const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
+              p4[u] = pe;
+              ds4[u] = pe * __uint_as_float(dr[e + u]);
+            }
+            pp[e / 2] = pack_half2(p4[0], p4[1]);
+            pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
+            dd[e / 2] = pack_half2(ds4[0], ds4[1]);
+            dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
+          }
         }
         if (cc == 0) {
           if (threadIdx.x == 0) TRACE(11, i);

@@ -381,9 +381,9 @@ __global__ void __launch_bounds__(544, 1)
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
         if (role <= 1) {
           // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
-          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc) ||
-              (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)))
-            break;
+          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc)) break;
+          if (role == 0) TRACE(15, i);
+          if (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)) break;
           if (role == 0) TRACE(2, i);
           if (role == 0 && i == 0) CTRACE(2);
           tc_fence_after();

@@ -49,6 +49,12 @@ def load() -> ctypes.CDLL:
                                          _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp,
                                          _vp]
             lib.fa_sm100_bwd.restype = _c_int
+            lib.fa_sm100_fwd_gqa.argtypes = [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                             _c_int, _c_int, _c_float, _c_int, _vp, _vp]
+            lib.fa_sm100_fwd_gqa.restype = _c_int
+            lib.fa_sm100_bwd_gqa.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 5 + [
+                _c_float, _c_int, _vp, _vp]
+            lib.fa_sm100_bwd_gqa.restype = _c_int
             lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes
             lib.fa_sm100_bwd_phase.restype = _c_int
             lib.fa_sm100_bwd_noalloc.argtypes = [_vp] * 9 + [_c_int] * 4 + [_c_float, _c_int,

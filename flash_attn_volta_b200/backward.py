@@ -13,7 +13,7 @@ import math
 import torch
 
 from . import _lib
-from .forward import _as_kernel_input
+from .forward import _as_kernel_input, _kv_heads
 
 
 def flash_attn_backward(
@@ -30,17 +30,20 @@ def flash_attn_backward(
 
     Args:
         do: (B, N, H, D) fp16, gradient w.r.t. output.
-        q, k, v, o: (B, N, H, D) fp16 forward inputs and output.
+        q, k, v, o: (B, N, H, D) fp16 forward inputs and output (k, v may have
+            H_kv heads, H % H_kv == 0, as in the forward).
         lse: (B, H, N) fp32 log-sum-exp from the forward (+inf on fully masked rows).
         causal, sm_scale: must match the forward call.
 
     Returns:
-        (dq, dk, dv), each (B, N, H, D) fp16.
+        (dq, dk, dv), fp16, shaped like q, k and v (dk, dv sum over the query
+        heads that share each K/V head).
     """
     assert q.is_cuda and k.is_cuda and v.is_cuda and o.is_cuda and do.is_cuda
     assert q.dtype == torch.float16 == k.dtype == v.dtype == o.dtype == do.dtype
     assert lse.dtype == torch.float32
-    assert q.shape == k.shape == v.shape == o.shape == do.shape
+    assert q.shape == o.shape == do.shape
+    Hkv = _kv_heads(q, k, v)
     B, N, H, D = q.shape
     assert D in (16, 32, 64, 128), f"unsupported head_dim {D}"
     assert lse.shape == (B, H, N), f"lse shape {lse.shape} expected ({B},{H},{N})"
@@ -51,8 +54,8 @@ def flash_attn_backward(
     do, q, k, v, o = (_as_kernel_input(t) for t in (do, q, k, v, o))
     lse = lse.contiguous()
     dq = torch.empty((B, N, H, D), dtype=torch.float16, device=q.device)
-    dk = torch.empty_like(dq)
-    dv = torch.empty_like(dq)
+    dk = torch.empty((B, N, Hkv, D), dtype=torch.float16, device=q.device)
+    dv = torch.empty_like(dk)
     if q.numel() == 0:
         return dq, dk, dv
     lib = _lib.load()
@@ -60,11 +63,11 @@ def flash_attn_backward(
     with _lib.on_device(idx):
         nbytes = lib.fa_sm100_bwd_workspace_bytes(B, N, H, D)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-        rc = lib.fa_sm100_bwd(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                              o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                              dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, D,
-                              float(sm_scale), 1 if causal else 0, _lib.status_ptr(idx),
-                              _lib.stream_ptr(idx))
+        rc = lib.fa_sm100_bwd_gqa(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                  o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                  dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, Hkv, D,
+                                  float(sm_scale), 1 if causal else 0, _lib.status_ptr(idx),
+                                  _lib.stream_ptr(idx))
     if rc:
         _lib.check(rc, "fa_sm100_bwd")
     if _lib.debug_sync():

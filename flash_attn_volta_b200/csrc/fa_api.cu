@@ -147,10 +147,14 @@ void fa_sm100_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 1u
 
 void fa_sm100_set_debug_flags(int flags) { g_debug_flags.store(flags); }
 
-int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
-                 int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
-                 void* stream) {
+}  // extern "C"
+
+namespace {
+int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
+             int seqlen, int nheads, int nheads_kv, int head_dim, float sm_scale, int causal,
+             int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
   if (!q || !k || !v || !out || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return FA_ERR_ARG;
   if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return FA_ERR_ARG;
@@ -158,8 +162,8 @@ int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* 
   if (rc != FA_OK) return rc;
   CUtensorMap tq, tk, tv;
   if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
   FwdArgs a;
   a.tm_q = &tq;
   a.tm_k = &tk;
@@ -169,6 +173,7 @@ int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* 
   a.B = batch;
   a.S = seqlen;
   a.H = nheads;
+  a.Hkv = nheads_kv;
   a.D = head_dim;
   a.scale = sm_scale;
   a.causal = causal ? 1 : 0;
@@ -176,6 +181,23 @@ int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* 
   a.timeout_ns = g_timeout_ns.load();
   a.debug_flags = g_debug_flags.load();
   return launch_fwd(a, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" {
+
+int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
+                 int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
+                 void* stream) {
+  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads, head_dim, sm_scale, causal,
+                  status, stream);
+}
+
+int fa_sm100_fwd_gqa(const void* q, const void* k, const void* v, void* out, float* lse,
+                     int batch, int seqlen, int nheads, int nheads_kv, int head_dim,
+                     float sm_scale, int causal, int* status, void* stream) {
+  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads_kv, head_dim, sm_scale, causal,
+                  status, stream);
 }
 
 size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim) {
@@ -188,9 +210,10 @@ size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_
 int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k,
                               const void* v, const void* out, const float* lse, void* dq, void* dk,
                               void* dv, void* workspace, size_t workspace_bytes, int batch, int seqlen,
-                              int nheads, int head_dim, float sm_scale, int causal, int* status,
-                              void* stream) {
+                              int nheads, int nheads_kv, int head_dim, float sm_scale, int causal,
+                              int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
   const void* ptrs[] = {dout, q, k, v, out, dq, dk, dv};
   for (const void* p : ptrs)
     if (!p || !aligned16(p)) return FA_ERR_ARG;
@@ -204,8 +227,8 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   CUtensorMap tq, tdo, tk, tv;
   if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
   if ((rc = make_bshd_map(&tdo, dout, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   BwdArgs a;
   a.tm_q = &tq;
@@ -226,6 +249,7 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   a.H = nheads;
   a.D = head_dim;
   a.S_pad = (int)round_up((size_t)seqlen, kSeqPad);
+  a.Hkv = nheads_kv;
   a.scale = sm_scale;
   a.causal = causal ? 1 : 0;
   a.status = status;
@@ -240,7 +264,16 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
                  float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, head_dim, sm_scale, causal, status, stream);
+                  seqlen, nheads, nheads, head_dim, sm_scale, causal, status, stream);
+}
+
+int fa_sm100_bwd_gqa(const void* dout, const void* q, const void* k, const void* v,
+                     const void* out, const float* lse, void* dq, void* dk, void* dv,
+                     void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
+                     int nheads_kv, int head_dim, float sm_scale, int causal, int* status,
+                     void* stream) {
+  return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
+                  seqlen, nheads, nheads_kv, head_dim, sm_scale, causal, status, stream);
 }
 
 int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
@@ -249,7 +282,7 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
                        int head_dim, float sm_scale, int causal, int* status, void* stream) {
   if (phase < 0 || phase > 2) return FA_ERR_ARG;
   return bwd_impl(phase, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, head_dim, sm_scale, causal, status, stream);
+                  seqlen, nheads, nheads, head_dim, sm_scale, causal, status, stream);
 }
 
 }  // extern "C"

@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(544, 1)
                        const __grid_constant__ CUtensorMap tm_v,
                        const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
                        float* __restrict__ dq_acc,
-                       __half* __restrict__ dk, __half* __restrict__ dv, int S, int H, int S_pad,
+                       __half* __restrict__ dk, __half* __restrict__ dv, int S, int H, int group,
+                       int S_pad,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
   using C = BwdCfg<D>;
@@ -259,16 +260,25 @@ __global__ void __launch_bounds__(544, 1)
     if (blockIdx.x < 8192) g_bcta[blockIdx.x][0] = smid;
 #endif
   }
-  // 1-D grid over (head group, key block, head): key block 0 (the most query
-  // tiles under a causal mask) first inside each group of heads
+  // 1-D grid over (head group, key block, K/V head): key block 0 (the most
+  // query tiles under a causal mask) first inside each group of heads.  With
+  // grouped-query attention (`group` query heads per K/V head) the CTA runs
+  // through every query head of its group, so dK / dV sum over the group in
+  // tensor memory.
   const int nkt = (S + C::BN - 1) / C::BN;
-  int bh, kt;
-  grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nkt), nkt, kHeadGroup, bh, kt);
-  const int b = bh / H, h = bh % H;
+  const int Hkv = H / group;
+  int bhk, kt;
+  grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nkt), nkt, kHeadGroup, bhk, kt);
+  const int b = bhk / Hkv, hk = bhk % Hkv;
   const int kv0 = kt * C::BN;
   const int ntq = (S + C::BM - 1) / C::BM;
   const int i0 = causal ? kv0 / C::BM : 0;  // first query tile that sees this key tile
-  const int nq = ntq - i0;
+  const int nq = ntq - i0;                  // query tiles per query head
+  const int nit = group * nq;               // iterations: (query head, query tile)
+  // iteration it: query head hk * group + it / nq, first row of query tile i0 + it % nq
+  // (no division for plain multi-head attention: it sits on the softmax warps' path)
+  auto q_head = [&](int it) { return group == 1 ? hk : hk * group + it / nq; };
+  auto q_row0 = [&](int it) { return (i0 + (group == 1 ? it : it % nq)) * C::BM; };
 
   WaitCtx wc{abort_flag, status, timeout_ns};
 
@@ -315,8 +325,8 @@ __global__ void __launch_bounds__(544, 1)
       tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(bar(C_KVFULL), 2 * C::KV_BYTES);
       for (int a = 0; a < C::NAT; ++a) {
-        tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, h, b);
-        tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, h, b);
+        tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, hk, b);
+        tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, hk, b);
       }
     }
     griddep_wait();
@@ -324,13 +334,13 @@ __global__ void __launch_bounds__(544, 1)
     if (lane == 0) {
       int q_last[C::NST];  // last query tile loaded into each stage
       for (int t = 0; t < C::NST; ++t) q_last[t] = -1;
-      for (int i = 0; i < nq; ++i) {
-        const int st = i % C::NST;
-        const uint32_t ph = (uint32_t)(i / C::NST) & 1u;
-        const int q0 = (i0 + i) * C::BM;
-        TRACE(0, i);
-        if (i >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
-        TRACE(1, i);
+      for (int it = 0; it < nit; ++it) {
+        const int st = it % C::NST;
+        const uint32_t ph = (uint32_t)(it / C::NST) & 1u;
+        const int q0 = q_row0(it), h = q_head(it);
+        TRACE(0, it);
+        if (it >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
+        TRACE(1, it);
         mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::AUG_BYTES);
         for (int a = 0; a < C::NAT; ++a) {
           tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
@@ -338,12 +348,12 @@ __global__ void __launch_bounds__(544, 1)
           tma_load_4d(sbase + C::OFF_DO + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_do,
                       bar(C_QFULL + st), a * C::AE, q0, h, b);
         }
-        const size_t aug = ((size_t)bh * S_pad + q0) * kAugRowBytes;
+        const size_t aug = ((size_t)(b * H + h) * S_pad + q0) * kAugRowBytes;
         bulk_load(sbase + C::OFF_QA + st * C::AUG_BYTES, q_aug + aug, C::AUG_BYTES,
                   bar(C_QFULL + st));
         bulk_load(sbase + C::OFF_DA + st * C::AUG_BYTES, do_aug + aug, C::AUG_BYTES,
                   bar(C_QFULL + st));
-        q_last[st] = i;
+        q_last[st] = it;
       }
       // After an abort, let the loads this CTA issued land before it exits.
       if (*abort_flag) {
@@ -375,17 +385,17 @@ __global__ void __launch_bounds__(544, 1)
       constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
                                         : make_idesc_f16(C::BM, D, true, true);  // dQ
       bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
-      for (int i = 0; ok && i < nq; ++i) {
-        const int st = i % C::NST;
+      for (int it = 0; ok && it < nit; ++it) {
+        const int st = it % C::NST;
         const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
         if (role <= 1) {
           // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
-          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc)) break;
-          if (role == 0) TRACE(15, i);
-          if (i > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(i - 1) & 1u, wc)) break;
-          if (role == 0) TRACE(2, i);
-          if (role == 0 && i == 0) CTRACE(2);
+          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(it / C::NST) & 1u, wc)) break;
+          if (role == 0) TRACE(15, it);
+          if (it > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(it - 1) & 1u, wc)) break;
+          if (role == 0) TRACE(2, it);
+          if (role == 0 && it == 0) CTRACE(2);
           tc_fence_after();
           const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
           const uint32_t bbase = role == 0 ? qb : dob;
@@ -404,39 +414,39 @@ __global__ void __launch_bounds__(544, 1)
                                     128, 256, 0),
                      id_s, 1u);
           mma_commit(bar(C_SFULL));
-          if (role == 0) TRACE(3, i);
+          if (role == 0) TRACE(3, it);
         } else if (role == 2) {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc)) break;
-          TRACE(4, i);
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)it & 1u, wc)) break;
+          TRACE(4, it);
           tc_fence_after();
           // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
 #pragma unroll
           for (int kk = 0; kk < C::BM / 16; ++kk) {
             const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-            mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
 #pragma unroll
           for (int kk = 0; kk < C::BM / 16; ++kk) {
             const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
             if constexpr (C::DS_TMEM) {
               mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
-                         (i > 0 || kk > 0) ? 1u : 0u);
+                         (it > 0 || kk > 0) ? 1u : 0u);
             } else {
               const int a = kk / 4;
               const uint32_t koff = (uint32_t)(kk % 4) * 32u;
               const uint64_t sd =
                   make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
-              mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (i > 0 || kk > 0) ? 1u : 0u);
+              mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
             }
           }
           mma_commit(bar(C_QEMPTY + st));
           mma_commit(bar(C_PFREE));
-          TRACE(6, i);
+          TRACE(6, it);
         } else {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)i & 1u, wc) ||
-              (i > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(i - 1) & 1u, wc)))
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)it & 1u, wc) ||
+              (it > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(it - 1) & 1u, wc)))
             break;
-          TRACE(5, i);
+          TRACE(5, it);
           tc_fence_after();
           // dQ partial over this key tile (K = 128 key rows)
 #pragma unroll
@@ -467,15 +477,15 @@ __global__ void __launch_bounds__(544, 1)
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
     const int c0 = hf * HW;          // first query column of this thread
     bool ok = true;
-    for (int i = 0; i < nq; ++i) {
-      const int st = i % C::NST;
-      const int q0 = (i0 + i) * C::BM;
-      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(i / C::NST) & 1u, wc) ||
-          !mbar_wait(bar(C_SFULL), (uint32_t)i & 1u, wc)) {
+    for (int it = 0; it < nit; ++it) {
+      const int st = it % C::NST;
+      const int q0 = q_row0(it);
+      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(it / C::NST) & 1u, wc) ||
+          !mbar_wait(bar(C_SFULL), (uint32_t)it & 1u, wc)) {
         ok = false;
         break;
       }
-      if (threadIdx.x == 0) TRACE(7, i);
+      if (threadIdx.x == 0) TRACE(7, it);
       tc_fence_after();
       // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
       // dP^T are released after the last chunk's loads; P^T / dS^T are written only
@@ -489,12 +499,12 @@ __global__ void __launch_bounds__(544, 1)
         tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
         tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
         tmem_wait_ld();
-        if (threadIdx.x == 0 && cc == 0) TRACE(14, i);
+        if (threadIdx.x == 0 && cc == 0) TRACE(14, it);
         if (cc == HW / 32 - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(C_SFREE));
-          if (threadIdx.x == 0) TRACE(8, i);
+          if (threadIdx.x == 0) TRACE(8, it);
         }
         // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
         // dP'^T already hold -LSE/scale and -delta).  Only tiles that cross the
@@ -534,12 +544,12 @@ __global__ void __launch_bounds__(544, 1)
           }
         }
         if (cc == 0) {
-          if (threadIdx.x == 0) TRACE(11, i);
-          if (i > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(i - 1) & 1u, wc)) {
+          if (threadIdx.x == 0) TRACE(11, it);
+          if (it > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(it - 1) & 1u, wc)) {
             ok = false;
             break;
           }
-          if (threadIdx.x == 0) TRACE(9, i);
+          if (threadIdx.x == 0) TRACE(9, it);
         }
         // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
         // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
@@ -559,14 +569,14 @@ __global__ void __launch_bounds__(544, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C_DSREADY));
-      if (threadIdx.x == 0) TRACE(10, i);
+      if (threadIdx.x == 0) TRACE(10, it);
     }
     // ------------------------------------------------------------ dK / dV epilogue
     constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
     if (ok && hf * EC < D && mbar_wait(bar(C_KVDONE), 0, wc)) {
       tc_fence_after();
-      __half* dvrow = dv + (((size_t)b * S + kv_idx) * H + h) * D;
-      __half* dkrow = dk + (((size_t)b * S + kv_idx) * H + h) * D;
+      __half* dvrow = dv + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
+      __half* dkrow = dk + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
         const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
@@ -600,12 +610,13 @@ __global__ void __launch_bounds__(544, 1)
     const int wq = warp - 8;
     const int tid = threadIdx.x - 256;  // 0..127
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    for (int i = 0; i < nq; ++i) {
-      const int q0 = (i0 + i) * C::BM;
-      const int sbuf = i % C::NDQ;
+    for (int it = 0; it < nit; ++it) {
+      const int q0 = q_row0(it);
+      const int bh = b * H + q_head(it);
+      const int sbuf = it % C::NDQ;
       const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
-      if (!mbar_wait(bar(C_DQFULL), (uint32_t)i & 1u, wc)) break;
-      if (tid == 0) TRACE(12, i);
+      if (!mbar_wait(bar(C_DQFULL), (uint32_t)it & 1u, wc)) break;
+      if (tid == 0) TRACE(12, it);
       tc_fence_after();
       if constexpr (C::DQT) {
         // TMEM lane = d, column = query row
@@ -664,7 +675,7 @@ __global__ void __launch_bounds__(544, 1)
       if (tid == 0) {
         bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
         bulk_commit_group();
-        TRACE(13, i);
+        TRACE(13, it);
       }
     }
     if (tid == 0) bulk_wait_group_all();
@@ -687,11 +698,12 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   using C = BwdCfg<D>;
   if (!smem_attr_set<1000 + D>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D>), C::SMEM))
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.H * ((a.S + C::BN - 1) / C::BN));
+  dim3 grid(a.B * a.Hkv * ((a.S + C::BN - 1) / C::BN));
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do, *a.tm_k,
       *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<__half*>(a.dk), static_cast<__half*>(a.dv),
-      a.S, a.H, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status, a.timeout_ns);
+      a.S, a.H, a.H / a.Hkv, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status,
+      a.timeout_ns);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

@@ -114,8 +114,8 @@ template <int D>
 __global__ void __launch_bounds__(640, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
-                  float* __restrict__ lse, int S, int H, float scale_log2, int causal, int* status,
-                  unsigned long long timeout_ns, int debug_flags) {
+                  float* __restrict__ lse, int S, int H, int group, float scale_log2, int causal,
+                  int* status, unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(640, 1)
   grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nblk), nblk, kHeadGroup, bh, rank);
   const int qt = causal ? (nblk - 1 - rank) : rank;
   const int b = bh / H, h = bh % H;
+  const int hk = h / group;  // K/V head (grouped-query attention: `group` query heads per K/V head)
   const int q0 = qt * C::BM;
   const int nkv_all = (S + C::BN - 1) / C::BN;
   const int nkv = causal ? min(nkv_all, (q0 + C::BM + C::BN - 1) / C::BN) : nkv_all;
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(640, 1)
         mbar_arrive_expect_tx(bar(B_KFULL + sk), C::KV_BYTES);
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
-                      bar(B_KFULL + sk), a * C::AE, j * C::BN, h, b);
+                      bar(B_KFULL + sk), a * C::AE, j * C::BN, hk, b);
         loaded = j + 1;
       }
       // After an abort, let the loads this thread issued land before the CTA exits.
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(640, 1)
         mbar_arrive_expect_tx(bar(B_VFULL + sv), C::KV_BYTES);
         for (int a = 0; a < C::NAT; ++a)
           tma_load_4d(sbase + C::OFF_V + sv * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
-                      bar(B_VFULL + sv), a * C::AE, j * C::BN, h, b);
+                      bar(B_VFULL + sv), a * C::AE, j * C::BN, hk, b);
       }
       if (*abort_flag) {
         for (int j = max(0, loaded - C::NSTV); j < loaded; ++j) {
@@ -467,8 +468,8 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
   const cudaError_t e = launch_pdl(fa_fwd_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream,
                                    *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse,
-                                   a.S, a.H, a.scale * 1.4426950408889634f, a.causal, a.status,
-                                   a.timeout_ns, a.debug_flags);
+                                   a.S, a.H, a.H / a.Hkv, a.scale * 1.4426950408889634f, a.causal,
+                                   a.status, a.timeout_ns, a.debug_flags);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

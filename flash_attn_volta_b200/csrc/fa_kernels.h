@@ -20,6 +20,7 @@ struct FwdArgs {
   void* o;
   float* lse;
   int B, S, H, D;
+  int Hkv;  // K/V heads (H % Hkv == 0; H for plain multi-head attention)
   float scale;
   int causal;
   int* status;
@@ -44,17 +45,22 @@ struct BwdArgs {
   uint8_t* q_aug;
   uint8_t* do_aug;
   int B, S, H, D, S_pad;
+  int Hkv;  // K/V heads (H % Hkv == 0); dk, dv are (B, S, Hkv, D)
   float scale;
   int causal;
   int* status;
   unsigned long long timeout_ns;
 };
 
+namespace {
 // Raise a kernel's dynamic shared-memory limit once per device (the attribute
 // is per device and function; setting it on every launch costs a driver call).
 // `Tag` separates the callers' kernels; devices beyond 64 are set every time.
+// Internal linkage: a function-local static of an inline function with external
+// linkage becomes one process-wide symbol, which a second copy of this library
+// loaded into the same process would share (and skip its own kernels' limits).
 template <int Tag>
-inline bool smem_attr_set(const void* func, int bytes) {
+bool smem_attr_set(const void* func, int bytes) {
   static std::atomic<unsigned long long> done{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -65,6 +71,7 @@ inline bool smem_attr_set(const void* func, int bytes) {
   done.fetch_or(bit, std::memory_order_acq_rel);
   return true;
 }
+}  // namespace
 
 // Launch with programmatic stream serialization: the kernel may start while the
 // previous kernel in the stream finishes (it calls griddep_wait() before reading
@@ -97,8 +104,10 @@ int bwd_q_rows(int D);
 // workspace (phase as in launch_bwd).  Shared by the C ABI entry points.
 int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
              const void* out, const float* lse, void* dq, void* dk, void* dv, void* workspace,
-             size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
-             float sm_scale, int causal, int* status, void* stream);  // query rows per backward iteration
+             size_t workspace_bytes, int batch, int seqlen, int nheads, int nheads_kv,
+             int head_dim, float sm_scale, int causal, int* status, void* stream);
+
+// sequence rows are padded to a multiple of this in the backward workspace
 constexpr int kSeqPad = 128;
 
 }  // namespace fa_sm100

@@ -25,6 +25,16 @@ def _as_kernel_input(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+def _kv_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> int:
+    """K/V head count: q's (multi-head) or a divisor of it (grouped-query /
+    multi-query attention: k and v are (B, N, H_kv, D)).  Anything else raises
+    the reference's AssertionError."""
+    ok = (k.shape == v.shape and q.dim() == 4 and k.dim() == 4 and q.shape[:2] == k.shape[:2]
+          and q.shape[3] == k.shape[3] and k.shape[2] > 0 and q.shape[2] % k.shape[2] == 0)
+    assert ok, f"qkv shape mismatch {q.shape} {k.shape} {v.shape}"
+    return k.shape[2]
+
+
 def _stream_ptr(device: torch.device) -> int:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     return _lib.stream_ptr(idx)
@@ -41,7 +51,9 @@ def flash_attn_forward(
     """FlashAttention forward on B200: fp16 in/out, fp32 accumulation.
 
     Args:
-        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.
+        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.  k and v
+                 may also have H_kv heads with H % H_kv == 0 (grouped-query or
+                 multi-query attention: query head h uses K/V head h // (H // H_kv)).
         causal:  if True apply the top-left lower-triangular mask.
         sm_scale: softmax scale (default 1/sqrt(D)).
         return_softmax_lse: if True also return the per-row log-sum-exp.
@@ -52,7 +64,7 @@ def flash_attn_forward(
     """
     assert q.is_cuda and k.is_cuda and v.is_cuda, "tensors must be on CUDA"
     assert q.dtype == torch.float16 == k.dtype == v.dtype, "fp16 only"
-    assert q.shape == k.shape == v.shape, f"qkv shape mismatch {q.shape} {k.shape} {v.shape}"
+    Hkv = _kv_heads(q, k, v)
     B, N, H, D = q.shape
     assert D in (16, 32, 64, 128), f"unsupported head_dim {D} (allowed: 16,32,64,128)"
     assert q.device == k.device == v.device, "q, k, v must be on the same device"
@@ -67,10 +79,10 @@ def flash_attn_forward(
         lib = _lib.load()
         idx = q.device.index
         with _lib.on_device(idx):
-            rc = lib.fa_sm100_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                                  lse.data_ptr() if lse is not None else None,
-                                  B, N, H, D, float(sm_scale), 1 if causal else 0,
-                                  _lib.status_ptr(idx), _lib.stream_ptr(idx))
+            rc = lib.fa_sm100_fwd_gqa(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                      lse.data_ptr() if lse is not None else None,
+                                      B, N, H, Hkv, D, float(sm_scale), 1 if causal else 0,
+                                      _lib.status_ptr(idx), _lib.stream_ptr(idx))
         if rc:
             _lib.check(rc, "fa_sm100_fwd")
         if _lib.debug_sync():

@@ -22,8 +22,9 @@ only for square self-attention (prefill / training; ``q_len == kv_len``) with no
 mask or a pure causal mask, no attention-probability output, no attention
 dropout, no sliding window and a supported head_dim on CUDA; anything else (a
 KV-cache decode step, padding masks, cross-attention, ...) goes to the model's
-original attention implementation.  GQA/MQA K/V heads are expanded to the
-query heads as HF's ``repeat_kv`` does (patch_hf.py:187-188).
+original attention implementation.  GQA/MQA K/V go to the kernel with their
+own head count (query head h reads K/V head h // group), where the reference
+first expanded them to the query heads with ``repeat_kv`` (patch_hf.py:187-188).
 """
 from __future__ import annotations
 
@@ -81,14 +82,6 @@ def _original_attention(module, impl: str):
     return sys.modules[type(module).__module__].eager_attention_forward
 
 
-def _repeat_kv(x: torch.Tensor, n_rep: int) -> torch.Tensor:
-    """(B, Hkv, S, D) -> (B, Hkv * n_rep, S, D), each K/V head repeated n_rep times."""
-    if n_rep == 1:
-        return x
-    b, h, s, d = x.shape
-    return x[:, :, None].expand(b, h, n_rep, s, d).reshape(b, h * n_rep, s, d)
-
-
 def flash_attention_forward(module, query, key, value, attention_mask, scaling=None,
                             dropout: float = 0.0, **kwargs):
     """AttentionInterface function: (B, H, S, D) q/k/v -> ((B, S, H, D) out, None)."""
@@ -113,10 +106,9 @@ def flash_attention_forward(module, query, key, value, attention_mask, scaling=N
         fn = _original_attention(module, module._fa_orig_impl)
         return fn(module, query, key, value, attention_mask, scaling=scaling, dropout=dropout,
                   **kwargs)
-    n_rep = query.shape[1] // key.shape[1]
     q = query.transpose(1, 2).to(torch.float16)
-    k = _repeat_kv(key, n_rep).transpose(1, 2).to(torch.float16)
-    v = _repeat_kv(value, n_rep).transpose(1, 2).to(torch.float16)
+    k = key.transpose(1, 2).to(torch.float16)
+    v = value.transpose(1, 2).to(torch.float16)
     sm_scale = float(scaling) if scaling is not None else head_dim ** -0.5
     out = flash_attn(q, k, v, causal=True, sm_scale=sm_scale)
     return out.to(query.dtype), None

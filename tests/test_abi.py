@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert "fa_sm100_fwd" in names and "fa_sm100_bwd" in names
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/ but not exported"
-    assert lib.fa_sm100_abi_version() == 1
+    assert lib.fa_sm100_abi_version() == 2
 
 
 def test_error_strings():
@@ -77,3 +77,16 @@ def test_public_api_surface():
     assert set(m.__all__) == {"flash_attn_forward", "flash_attn_volta", "flash_attn_backward",
                               "flash_attn"}
     assert m.flash_attn_volta is m.flash_attn_forward
+
+
+def test_gqa_head_count_checks():
+    """fa_sm100_*_gqa reject a K/V head count that does not divide the query heads
+    before touching the device."""
+    lib = _lib.load()
+    args_f = (16, 16, 16, 16, None, 1, 64, 8, 3, 64, 0.125, 1, None, None)
+    assert lib.fa_sm100_fwd_gqa(*args_f) == _lib.FA_ERR_ARG
+    args_f0 = (16, 16, 16, 16, None, 1, 64, 8, 0, 64, 0.125, 1, None, None)
+    assert lib.fa_sm100_fwd_gqa(*args_f0) == _lib.FA_ERR_ARG
+    n = lib.fa_sm100_bwd_workspace_bytes(1, 64, 8, 64)
+    rc = lib.fa_sm100_bwd_gqa(*([256] * 9), 256, n, 1, 64, 8, 3, 64, 0.125, 1, None, None)
+    assert rc == _lib.FA_ERR_ARG

@@ -18,6 +18,9 @@ FAMILIES = ["llama", "qwen2", "qwen3", "gpt2"]
 
 
 def _oracle_flash_attn(q, k, v, causal=False, sm_scale=None):
+    # the kernel's grouped-query contract: query head h reads K/V head h // group
+    g = q.shape[2] // k.shape[2]
+    k, v = k.repeat_interleave(g, dim=2), v.repeat_interleave(g, dim=2)
     o, _ = attention_fwd(q.float(), k.float(), v.float(), causal=causal, scale=sm_scale)
     return o.to(q.dtype)
 
@@ -27,7 +30,7 @@ def cpu_fast_path(monkeypatch):
     calls = []
 
     def fake(q, k, v, causal=False, sm_scale=None):
-        calls.append((tuple(q.shape), causal, sm_scale))
+        calls.append((tuple(q.shape), causal, sm_scale, k.shape[2]))
         return _oracle_flash_attn(q, k, v, causal, sm_scale)
 
     monkeypatch.setattr(patch_hf, "flash_attn", fake)
@@ -59,8 +62,9 @@ def test_gqa_and_scale_forwarded(cpu_fast_path):
     patch_hf.patch_llama(model)
     with torch.no_grad():
         model(torch.randint(0, 128, (1, 10)))
-    shape, causal, scale = cpu_fast_path[0]
-    assert shape == (1, 10, 4, 32)  # 2 K/V heads expanded to the 4 query heads
+    shape, causal, scale, kv_heads = cpu_fast_path[0]
+    assert shape == (1, 10, 4, 32)
+    assert kv_heads == 2  # the 2 K/V heads reach the kernel unexpanded (grouped-query path)
     assert scale == pytest.approx(1 / math.sqrt(32))
 
 

@@ -23,6 +23,15 @@ FA_ERR_SCRATCH_LIMIT = 6
 
 STATUS_TIMEOUT = 1
 
+DTYPE_F16 = 0
+DTYPE_BF16 = 1
+_DTYPES = {torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    """FA_DTYPE_* of a torch dtype (fp16 or bf16)."""
+    return _DTYPES[dt]
+
 _lock = threading.Lock()
 _lib = None
 
@@ -49,12 +58,11 @@ def load() -> ctypes.CDLL:
                                          _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp,
                                          _vp]
             lib.fa_sm100_bwd.restype = _c_int
-            lib.fa_sm100_fwd_gqa.argtypes = [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
-                                             _c_int, _c_int, _c_float, _c_int, _vp, _vp]
-            lib.fa_sm100_fwd_gqa.restype = _c_int
-            lib.fa_sm100_bwd_gqa.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 5 + [
+            lib.fa_sm100_fwd_ex.argtypes = [_vp] * 5 + [_c_int] * 6 + [_c_float, _c_int, _vp, _vp]
+            lib.fa_sm100_fwd_ex.restype = _c_int
+            lib.fa_sm100_bwd_ex.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 6 + [
                 _c_float, _c_int, _vp, _vp]
-            lib.fa_sm100_bwd_gqa.restype = _c_int
+            lib.fa_sm100_bwd_ex.restype = _c_int
             lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes
             lib.fa_sm100_bwd_phase.restype = _c_int
             lib.fa_sm100_bwd_noalloc.argtypes = [_vp] * 9 + [_c_int] * 4 + [_c_float, _c_int,

@@ -26,10 +26,10 @@ def flash_attn_backward(
     causal: bool = False,
     sm_scale: float | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """FlashAttention backward on B200 — fp16 in/out, fp32 accumulation.
+    """FlashAttention backward on B200 — fp16 (or bf16) in/out, fp32 accumulation.
 
     Args:
-        do: (B, N, H, D) fp16, gradient w.r.t. output.
+        do: (B, N, H, D) gradient w.r.t. output, q's dtype (fp16 or bf16).
         q, k, v, o: (B, N, H, D) fp16 forward inputs and output (k, v may have
             H_kv heads, H % H_kv == 0, as in the forward).
         lse: (B, H, N) fp32 log-sum-exp from the forward (+inf on fully masked rows).
@@ -40,7 +40,8 @@ def flash_attn_backward(
         heads that share each K/V head).
     """
     assert q.is_cuda and k.is_cuda and v.is_cuda and o.is_cuda and do.is_cuda
-    assert q.dtype == torch.float16 == k.dtype == v.dtype == o.dtype == do.dtype
+    assert q.dtype in (torch.float16, torch.bfloat16)
+    assert q.dtype == k.dtype == v.dtype == o.dtype == do.dtype
     assert lse.dtype == torch.float32
     assert q.shape == o.shape == do.shape
     Hkv = _kv_heads(q, k, v)
@@ -53,8 +54,8 @@ def flash_attn_backward(
 
     do, q, k, v, o = (_as_kernel_input(t) for t in (do, q, k, v, o))
     lse = lse.contiguous()
-    dq = torch.empty((B, N, H, D), dtype=torch.float16, device=q.device)
-    dk = torch.empty((B, N, Hkv, D), dtype=torch.float16, device=q.device)
+    dq = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
+    dk = torch.empty((B, N, Hkv, D), dtype=q.dtype, device=q.device)
     dv = torch.empty_like(dk)
     if q.numel() == 0:
         return dq, dk, dv
@@ -63,11 +64,11 @@ def flash_attn_backward(
     with _lib.on_device(idx):
         nbytes = lib.fa_sm100_bwd_workspace_bytes(B, N, H, D)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-        rc = lib.fa_sm100_bwd_gqa(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                  o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                  dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, Hkv, D,
-                                  float(sm_scale), 1 if causal else 0, _lib.status_ptr(idx),
-                                  _lib.stream_ptr(idx))
+        rc = lib.fa_sm100_bwd_ex(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                 o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                 dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, Hkv, D,
+                                 _lib.dtype_code(q.dtype), float(sm_scale), 1 if causal else 0,
+                                 _lib.status_ptr(idx), _lib.stream_ptr(idx))
     if rc:
         _lib.check(rc, "fa_sm100_bwd")
     if _lib.debug_sync():

@@ -78,7 +78,8 @@ bool valid_shape(int B, int S, int H, int D) {
 
 // Tensor map over a contiguous (B, S, H, D) fp16 tensor; a box is `rows`
 // consecutive sequence positions of one (b, h) and one swizzle-width slice of D.
-int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, int rows) {
+int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, int rows,
+                  int dtype) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DEVICE;
   const int swb = D * 2 >= 128 ? 128 : D * 2;
@@ -90,7 +91,9 @@ int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, i
   const CUtensorMapSwizzle swz = swb == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                              : CU_TENSOR_MAP_SWIZZLE_32B;
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims,
+  const CUtensorMapDataType ty =
+      dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = enc(m, ty, 4, const_cast<void*>(ptr), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS && std::getenv("FA_SM100_DEBUG")) {
@@ -151,19 +154,23 @@ void fa_sm100_set_debug_flags(int flags) { g_debug_flags.store(flags); }
 
 namespace {
 int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
-             int seqlen, int nheads, int nheads_kv, int head_dim, float sm_scale, int causal,
-             int* status, void* stream) {
+             int seqlen, int nheads, int nheads_kv, int head_dim, int dtype, float sm_scale,
+             int causal, int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
   if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_ARG;
   if (!q || !k || !v || !out || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return FA_ERR_ARG;
   if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return FA_ERR_ARG;
   int rc = check_device();
   if (rc != FA_OK) return rc;
   CUtensorMap tq, tk, tv;
-  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, 128, dtype)) != FA_OK)
+    return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+    return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+    return rc;
   FwdArgs a;
   a.tm_q = &tq;
   a.tm_k = &tk;
@@ -174,6 +181,7 @@ int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse,
   a.S = seqlen;
   a.H = nheads;
   a.Hkv = nheads_kv;
+  a.dtype = dtype;
   a.D = head_dim;
   a.scale = sm_scale;
   a.causal = causal ? 1 : 0;
@@ -189,15 +197,15 @@ extern "C" {
 int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
                  int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
                  void* stream) {
-  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads, head_dim, sm_scale, causal,
-                  status, stream);
+  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16,
+                  sm_scale, causal, status, stream);
 }
 
-int fa_sm100_fwd_gqa(const void* q, const void* k, const void* v, void* out, float* lse,
-                     int batch, int seqlen, int nheads, int nheads_kv, int head_dim,
-                     float sm_scale, int causal, int* status, void* stream) {
-  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads_kv, head_dim, sm_scale, causal,
-                  status, stream);
+int fa_sm100_fwd_ex(const void* q, const void* k, const void* v, void* out, float* lse,
+                    int batch, int seqlen, int nheads, int nheads_kv, int head_dim, int dtype,
+                    float sm_scale, int causal, int* status, void* stream) {
+  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads_kv, head_dim, dtype, sm_scale,
+                  causal, status, stream);
 }
 
 size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim) {
@@ -210,10 +218,11 @@ size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_
 int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k,
                               const void* v, const void* out, const float* lse, void* dq, void* dk,
                               void* dv, void* workspace, size_t workspace_bytes, int batch, int seqlen,
-                              int nheads, int nheads_kv, int head_dim, float sm_scale, int causal,
-                              int* status, void* stream) {
+                              int nheads, int nheads_kv, int head_dim, int dtype, float sm_scale,
+                              int causal, int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
   if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_ARG;
   const void* ptrs[] = {dout, q, k, v, out, dq, dk, dv};
   for (const void* p : ptrs)
     if (!p || !aligned16(p)) return FA_ERR_ARG;
@@ -225,10 +234,14 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   if (rc != FA_OK) return rc;
   const int qrows = bwd_q_rows(head_dim);
   CUtensorMap tq, tdo, tk, tv;
-  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tdo, dout, batch, seqlen, nheads, head_dim, qrows)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128)) != FA_OK) return rc;
+  if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, qrows, dtype)) != FA_OK)
+    return rc;
+  if ((rc = make_bshd_map(&tdo, dout, batch, seqlen, nheads, head_dim, qrows, dtype)) != FA_OK)
+    return rc;
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+    return rc;
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+    return rc;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   BwdArgs a;
   a.tm_q = &tq;
@@ -250,6 +263,7 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   a.D = head_dim;
   a.S_pad = (int)round_up((size_t)seqlen, kSeqPad);
   a.Hkv = nheads_kv;
+  a.dtype = dtype;
   a.scale = sm_scale;
   a.causal = causal ? 1 : 0;
   a.status = status;
@@ -264,16 +278,17 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
                  float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads, head_dim, sm_scale, causal, status, stream);
+                  seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
+                  stream);
 }
 
-int fa_sm100_bwd_gqa(const void* dout, const void* q, const void* k, const void* v,
-                     const void* out, const float* lse, void* dq, void* dk, void* dv,
-                     void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
-                     int nheads_kv, int head_dim, float sm_scale, int causal, int* status,
-                     void* stream) {
+int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* v,
+                    const void* out, const float* lse, void* dq, void* dk, void* dv,
+                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
+                    int nheads_kv, int head_dim, int dtype, float sm_scale, int causal,
+                    int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads_kv, head_dim, sm_scale, causal, status, stream);
+                  seqlen, nheads, nheads_kv, head_dim, dtype, sm_scale, causal, status, stream);
 }
 
 int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
@@ -282,7 +297,8 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
                        int head_dim, float sm_scale, int causal, int* status, void* stream) {
   if (phase < 0 || phase > 2) return FA_ERR_ARG;
   return bwd_impl(phase, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads, head_dim, sm_scale, causal, status, stream);
+                  seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
+                  stream);
 }
 
 }  // extern "C"

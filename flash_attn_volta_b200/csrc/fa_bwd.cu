@@ -41,8 +41,11 @@
 //                partial = dS K (stored transposed for D=128).
 //   fa_bwd_post  dQ = fp16(scale * accumulator) in (B, S, H, D).
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "fa_kernels.h"
 #include "sm100_ptx.cuh"
@@ -140,22 +143,28 @@ __host__ __device__ constexpr uint32_t aug_offset(uint32_t row, uint32_t k) {
   return (row / 8) * 256 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2;
 }
 
-// x as an fp16 pair with hi + lo == x to ~2^-22 |x| (hi clamped to the fp16
-// range; a non-finite x, i.e. a fully masked row, becomes a large negative
-// term that drives every P of the row to zero).
-__device__ __forceinline__ uint32_t split_half2(float x) {
+// x as three terms of the element type, t0 + t1 + t2 == x to ~2^-22 |x| for fp16
+// and ~2^-24 |x| for bf16 (t0 clamped to the fp16 range; a non-finite x, i.e. a
+// fully masked row, becomes a large negative term that drives every P of the
+// row to zero); returned as the first 16-byte half of an extra-K-step row,
+// [t0, t1, t2, 0, 0, 0, 0, 0].
+template <typename T>
+__device__ __forceinline__ uint4 split_row(float x) {
   if (!(fabsf(x) <= 60000.f)) x = (x > 0.f) ? 60000.f : -60000.f;
-  const __half hi = __float2half_rn(x);
-  const __half lo = __float2half_rn(x - __half2float(hi));
-  return (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+  const uint16_t b0 = Elem<T>::bits(x);
+  const float r1 = x - Elem<T>::value(b0);
+  const uint16_t b1 = Elem<T>::bits(r1);
+  const uint16_t b2 = Elem<T>::bits(r1 - Elem<T>::value(b1));
+  return make_uint4((uint32_t)b0 | ((uint32_t)b1 << 16), (uint32_t)b2, 0u, 0u);
 }
 
 // D/8 threads per (bh, row) of the padded row range, 16-byte loads of O and dO:
-// delta = rowsum(O * dO); the row's extra K-step entries [hi, lo, 0, ...] of
+// delta = rowsum(O * dO); the row's extra K-step entries [t0, t1, t2, 0, ...] of
 // -LSE/scale (Q side) and -delta (dO side); the row of the fp32 dQ accumulator
 // zeroed.
+template <typename T>
 __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
-    const __half* __restrict__ o, const __half* __restrict__ dout, const float* __restrict__ lse,
+    const T* __restrict__ o, const T* __restrict__ dout, const float* __restrict__ lse,
     uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc, int S,
     int H, int D, int S_pad, float inv_scale) {
   griddep_wait();  // O and LSE come from the forward
@@ -176,8 +185,8 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&ow[i]));
-      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&dw[i]));
+      const float2 a = Elem<T>::unpack2(ow[i]);
+      const float2 c = Elem<T>::unpack2(dw[i]);
       acc = fmaf(a.x, c.x, acc);
       acc = fmaf(a.y, c.y, acc);
     }
@@ -189,11 +198,9 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     // row blocks of S_pad rows per (batch, head); S_pad is a multiple of 8
     const size_t base = (size_t)bh * S_pad * kAugRowBytes;
     const uint32_t r = (uint32_t)row;
-    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 0)) =
-        make_uint4(split_half2(-l * inv_scale), 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 0)) = split_row<T>(-l * inv_scale);
     *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) =
-        make_uint4(split_half2(-acc), 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) = split_row<T>(-acc);
     *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
   }
   float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
@@ -202,7 +209,8 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
 }
 
 // -------------------------------------------------------------------------- post
-__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __restrict__ dq, int S,
+template <typename T>
+__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restrict__ dq, int S,
                                    int H, int D, int S_pad, float scale) {
   // one thread per 8 consecutive elements of one (b, s, h) row
   griddep_wait();  // the dQ accumulator comes from the main kernel
@@ -220,15 +228,15 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __half* __r
   const float4 x0 = *reinterpret_cast<const float4*>(src);
   const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
   uint4 w;
-  w.x = pack_half2(x0.x * scale, x0.y * scale);
-  w.y = pack_half2(x0.z * scale, x0.w * scale);
-  w.z = pack_half2(x1.x * scale, x1.y * scale);
-  w.w = pack_half2(x1.z * scale, x1.w * scale);
+  w.x = Elem<T>::pack2(x0.x * scale, x0.y * scale);
+  w.y = Elem<T>::pack2(x0.z * scale, x0.w * scale);
+  w.z = Elem<T>::pack2(x1.x * scale, x1.y * scale);
+  w.w = Elem<T>::pack2(x1.z * scale, x1.w * scale);
   *reinterpret_cast<uint4*>(dq + (((size_t)b * S + r) * H + h) * D + e) = w;
 }
 
 // -------------------------------------------------------------------------- main
-template <int D>
+template <int D, typename T>
 __global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(544, 1)
                        const __grid_constant__ CUtensorMap tm_v,
                        const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
                        float* __restrict__ dq_acc,
-                       __half* __restrict__ dk, __half* __restrict__ dv, int S, int H, int group,
+                       T* __restrict__ dk, T* __restrict__ dv, int S, int H, int group,
                        int S_pad,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
@@ -298,9 +306,10 @@ __global__ void __launch_bounds__(544, 1)
     tmem_relinquish();
   }
   if (warp >= 8 && warp < 12) {
-    // the extra K-step rows of K and V: [1, 1, 0, ...] for each of the 128 key rows
+    // the extra K-step rows of K and V: [1, 1, 1, 0, ...] for each of the 128 key rows
     const uint32_t r = threadIdx.x - 256;
-    st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 0), 0x3C003C00u, 0u, 0u, 0u);
+    st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 0), Elem<T>::kOne | (Elem<T>::kOne << 16),
+                 Elem<T>::kOne, 0u, 0u);
     st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 8), 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
   }
@@ -380,10 +389,11 @@ __global__ void __launch_bounds__(544, 1)
     const int role = warp - 13;
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
-      constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false);   // S^T, dP^T
-      constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true);       // dV, dK
-      constexpr uint32_t id_dq = C::DQT ? make_idesc_f16(D, C::BM, true, true)   // dQ^T
-                                        : make_idesc_f16(C::BM, D, true, true);  // dQ
+      constexpr uint32_t ab = Elem<T>::kIdescAB;
+      constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false) | ab;  // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true) | ab;      // dV, dK
+      constexpr uint32_t id_dq = (C::DQT ? make_idesc_f16(D, C::BM, true, true)    // dQ^T
+                                         : make_idesc_f16(C::BM, D, true, true)) | ab;  // dQ
       bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
       for (int it = 0; ok && it < nit; ++it) {
         const int st = it % C::NST;
@@ -522,8 +532,8 @@ __global__ void __launch_bounds__(544, 1)
             f2_unpack(f2_mul(f2_pack(p0, p1),
                              f2_pack(__uint_as_float(dr[2 * k]), __uint_as_float(dr[2 * k + 1]))),
                       d0, d1);
-            pp[k] = pack_half2(p0, p1);
-            dd[k] = pack_half2(d0, d1);
+            pp[k] = Elem<T>::pack2(p0, p1);
+            dd[k] = Elem<T>::pack2(d0, d1);
           }
         } else {
 #pragma unroll
@@ -537,10 +547,10 @@ __global__ void __launch_bounds__(544, 1)
               p4[u] = pe;
               ds4[u] = pe * __uint_as_float(dr[e + u]);
             }
-            pp[e / 2] = pack_half2(p4[0], p4[1]);
-            pp[e / 2 + 1] = pack_half2(p4[2], p4[3]);
-            dd[e / 2] = pack_half2(ds4[0], ds4[1]);
-            dd[e / 2 + 1] = pack_half2(ds4[2], ds4[3]);
+            pp[e / 2] = Elem<T>::pack2(p4[0], p4[1]);
+            pp[e / 2 + 1] = Elem<T>::pack2(p4[2], p4[3]);
+            dd[e / 2] = Elem<T>::pack2(ds4[0], ds4[1]);
+            dd[e / 2 + 1] = Elem<T>::pack2(ds4[2], ds4[3]);
           }
         }
         if (cc == 0) {
@@ -575,27 +585,27 @@ __global__ void __launch_bounds__(544, 1)
     constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
     if (ok && hf * EC < D && mbar_wait(bar(C_KVDONE), 0, wc)) {
       tc_fence_after();
-      __half* dvrow = dv + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
-      __half* dkrow = dk + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
+      T* dvrow = dv + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
+      T* dkrow = dk + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
         const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
         const float f = pass == 0 ? 1.f : scale;
-        __half* dst = (pass == 0 ? dvrow : dkrow) + hf * EC;
+        T* dst = (pass == 0 ? dvrow : dkrow) + hf * EC;
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
           uint32_t v[16];
           tmem_ld16(tmem + lane_base + col + c * 16, v);
           tmem_wait_ld();
           uint4 w0, w1;
-          w0.x = pack_half2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
-          w0.y = pack_half2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
-          w0.z = pack_half2(__uint_as_float(v[4]) * f, __uint_as_float(v[5]) * f);
-          w0.w = pack_half2(__uint_as_float(v[6]) * f, __uint_as_float(v[7]) * f);
-          w1.x = pack_half2(__uint_as_float(v[8]) * f, __uint_as_float(v[9]) * f);
-          w1.y = pack_half2(__uint_as_float(v[10]) * f, __uint_as_float(v[11]) * f);
-          w1.z = pack_half2(__uint_as_float(v[12]) * f, __uint_as_float(v[13]) * f);
-          w1.w = pack_half2(__uint_as_float(v[14]) * f, __uint_as_float(v[15]) * f);
+          w0.x = Elem<T>::pack2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
+          w0.y = Elem<T>::pack2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
+          w0.z = Elem<T>::pack2(__uint_as_float(v[4]) * f, __uint_as_float(v[5]) * f);
+          w0.w = Elem<T>::pack2(__uint_as_float(v[6]) * f, __uint_as_float(v[7]) * f);
+          w1.x = Elem<T>::pack2(__uint_as_float(v[8]) * f, __uint_as_float(v[9]) * f);
+          w1.y = Elem<T>::pack2(__uint_as_float(v[10]) * f, __uint_as_float(v[11]) * f);
+          w1.z = Elem<T>::pack2(__uint_as_float(v[12]) * f, __uint_as_float(v[13]) * f);
+          w1.w = Elem<T>::pack2(__uint_as_float(v[14]) * f, __uint_as_float(v[15]) * f);
           if (kv_ok) {
             reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
             reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
@@ -693,15 +703,16 @@ __global__ void __launch_bounds__(544, 1)
   }
 }
 
-template <int D>
+template <int D, typename T>
 static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   using C = BwdCfg<D>;
-  if (!smem_attr_set<1000 + D>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D>), C::SMEM))
+  constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000);
+  if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.Hkv * ((a.S + C::BN - 1) / C::BN));
   const cudaError_t e = launch_pdl(
-      fa_bwd_main_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do, *a.tm_k,
-      *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<__half*>(a.dk), static_cast<__half*>(a.dv),
+      fa_bwd_main_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
+      *a.tm_k, *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<T*>(a.dk), static_cast<T*>(a.dv),
       a.S, a.H, a.H / a.Hkv, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status,
       a.timeout_ns);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
@@ -709,21 +720,22 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
 
 int bwd_q_rows(int D) { return D == 128 ? 64 : 128; }
 
-int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
+template <typename T>
+static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream, int phase) {
   if (phase < 0 || phase == 0) {
     const int rows_per_block = 256 / (a.D / 8);
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
-    if (launch_pdl(fa_bwd_pre_kernel, grid, dim3(256), 0, stream, static_cast<const __half*>(a.o),
-                   static_cast<const __half*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.S,
-                   a.H, a.D, a.S_pad, 1.0f / a.scale) != cudaSuccess)
+    if (launch_pdl(fa_bwd_pre_kernel<T>, grid, dim3(256), 0, stream, static_cast<const T*>(a.o),
+                   static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.S, a.H,
+                   a.D, a.S_pad, 1.0f / a.scale) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   int rc = FA_OK;
   if (phase < 0 || phase == 1) switch (a.D) {
-    case 16: rc = launch_bwd_main<16>(a, stream); break;
-    case 32: rc = launch_bwd_main<32>(a, stream); break;
-    case 64: rc = launch_bwd_main<64>(a, stream); break;
-    case 128: rc = launch_bwd_main<128>(a, stream); break;
+    case 16: rc = launch_bwd_main<16, T>(a, stream); break;
+    case 32: rc = launch_bwd_main<32, T>(a, stream); break;
+    case 64: rc = launch_bwd_main<64, T>(a, stream); break;
+    case 128: rc = launch_bwd_main<128, T>(a, stream); break;
     default: return FA_ERR_ARG;
   }
   if (rc != FA_OK) return rc;
@@ -731,11 +743,16 @@ int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
     const int per_row = a.D / 8;
     const size_t n = (size_t)a.S * per_row;
     dim3 grid((unsigned)((n + 255) / 256), a.B * a.H);
-    if (launch_pdl(fa_bwd_post_kernel, grid, dim3(256), 0, stream, a.dq_acc,
-                   static_cast<__half*>(a.dq), a.S, a.H, a.D, a.S_pad, a.scale) != cudaSuccess)
+    if (launch_pdl(fa_bwd_post_kernel<T>, grid, dim3(256), 0, stream, a.dq_acc,
+                   static_cast<T*>(a.dq), a.S, a.H, a.D, a.S_pad, a.scale) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   return FA_OK;
+}
+
+int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase) {
+  return a.dtype == FA_DTYPE_BF16 ? launch_bwd_t<__nv_bfloat16>(a, stream, phase)
+                                  : launch_bwd_t<__half>(a, stream, phase);
 }
 
 }  // namespace fa_sm100

@@ -35,8 +35,11 @@
 // masked, triton_fa.py:124-126), columns >= S masked (:123), LSE = m + ln(l)
 // and +inf for a row with l == 0 (:152-159), rows >= S not stored (:149-150).
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "fa_kernels.h"
 #include "sm100_ptx.cuh"
@@ -110,10 +113,10 @@ enum FwdBar {
   B_COUNT = 31
 };
 
-template <int D>
+template <int D, typename T>
 __global__ void __launch_bounds__(640, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
+                  const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
                   float* __restrict__ lse, int S, int H, int group, float scale_log2, int causal,
                   int* status, unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(640, 1)
   } else if (warp == 17) {
     // ------------------------------------------------------------ S issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = make_idesc_f16(C::BM, C::BN, false, false);
+      constexpr uint32_t idesc_qk = make_idesc_f16(C::BM, C::BN, false, false) | Elem<T>::kIdescAB;
       constexpr uint32_t swz = swizzle_field(C::SWB);
       bool ok = mbar_wait(bar(B_QFULL), 0, wc);
       for (int j = 0; ok && j < nkv; ++j) {
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(640, 1)
   } else if (warp == 18) {
     // ------------------------------------------------------------ PV issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_pv = make_idesc_f16(C::BM, D, false, true);
+      constexpr uint32_t idesc_pv = make_idesc_f16(C::BM, D, false, true) | Elem<T>::kIdescAB;
       constexpr uint32_t swz = swizzle_field(C::SWB);
       bool ok = true;
       for (int j = 0; ok && j < nkv; ++j) {
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(640, 1)
         sum2 = f2_add(sum2, p2);
         float p0, p1;
         f2_unpack(p2, p0, p1);
-        pp[k] = pack_half2(p0, p1);
+        pp[k] = Elem<T>::pack2(p0, p1);
       }
       float lsum0, lsum1;
       f2_unpack(sum2, lsum0, lsum1);
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(640, 1)
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = q_idx < S;
-      __half* orow = out + (((size_t)b * S + q_idx) * H + h) * D + cq * EC;
+      T* orow = out + (((size_t)b * S + q_idx) * H + h) * D + cq * EC;
       if (o_cols) {
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
@@ -426,14 +429,14 @@ __global__ void __launch_bounds__(640, 1)
           tmem_ld16(tmem + lane_base + C::COL_O + cq * EC + c * 16, o);
           tmem_wait_ld();
           uint4 w0, w1;
-          w0.x = pack_half2(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
-          w0.y = pack_half2(__uint_as_float(o[2]) * inv_l, __uint_as_float(o[3]) * inv_l);
-          w0.z = pack_half2(__uint_as_float(o[4]) * inv_l, __uint_as_float(o[5]) * inv_l);
-          w0.w = pack_half2(__uint_as_float(o[6]) * inv_l, __uint_as_float(o[7]) * inv_l);
-          w1.x = pack_half2(__uint_as_float(o[8]) * inv_l, __uint_as_float(o[9]) * inv_l);
-          w1.y = pack_half2(__uint_as_float(o[10]) * inv_l, __uint_as_float(o[11]) * inv_l);
-          w1.z = pack_half2(__uint_as_float(o[12]) * inv_l, __uint_as_float(o[13]) * inv_l);
-          w1.w = pack_half2(__uint_as_float(o[14]) * inv_l, __uint_as_float(o[15]) * inv_l);
+          w0.x = Elem<T>::pack2(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
+          w0.y = Elem<T>::pack2(__uint_as_float(o[2]) * inv_l, __uint_as_float(o[3]) * inv_l);
+          w0.z = Elem<T>::pack2(__uint_as_float(o[4]) * inv_l, __uint_as_float(o[5]) * inv_l);
+          w0.w = Elem<T>::pack2(__uint_as_float(o[6]) * inv_l, __uint_as_float(o[7]) * inv_l);
+          w1.x = Elem<T>::pack2(__uint_as_float(o[8]) * inv_l, __uint_as_float(o[9]) * inv_l);
+          w1.y = Elem<T>::pack2(__uint_as_float(o[10]) * inv_l, __uint_as_float(o[11]) * inv_l);
+          w1.z = Elem<T>::pack2(__uint_as_float(o[12]) * inv_l, __uint_as_float(o[13]) * inv_l);
+          w1.w = Elem<T>::pack2(__uint_as_float(o[14]) * inv_l, __uint_as_float(o[15]) * inv_l);
           if (row_ok) {
             reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
             reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
@@ -460,27 +463,34 @@ __global__ void __launch_bounds__(640, 1)
   }
 }
 
-template <int D>
+template <int D, typename T>
 static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<D>;
-  if (!smem_attr_set<D>(reinterpret_cast<const void*>(fa_fwd_kernel<D>), C::SMEM))
+  constexpr int tag = D + (std::is_same<T, __half>::value ? 0 : 1000);
+  if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_fwd_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
   dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
-  const cudaError_t e = launch_pdl(fa_fwd_kernel<D>, grid, dim3(C::THREADS), C::SMEM, stream,
-                                   *a.tm_q, *a.tm_k, *a.tm_v, static_cast<__half*>(a.o), a.lse,
+  const cudaError_t e = launch_pdl(fa_fwd_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream,
+                                   *a.tm_q, *a.tm_k, *a.tm_v, static_cast<T*>(a.o), a.lse,
                                    a.S, a.H, a.H / a.Hkv, a.scale * 1.4426950408889634f, a.causal,
                                    a.status, a.timeout_ns, a.debug_flags);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
+template <typename T>
+static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   switch (a.D) {
-    case 16: return launch_fwd_d<16>(a, stream);
-    case 32: return launch_fwd_d<32>(a, stream);
-    case 64: return launch_fwd_d<64>(a, stream);
-    case 128: return launch_fwd_d<128>(a, stream);
+    case 16: return launch_fwd_d<16, T>(a, stream);
+    case 32: return launch_fwd_d<32, T>(a, stream);
+    case 64: return launch_fwd_d<64, T>(a, stream);
+    case 128: return launch_fwd_d<128, T>(a, stream);
     default: return FA_ERR_ARG;
   }
+}
+
+int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
+  return a.dtype == FA_DTYPE_BF16 ? launch_fwd_t<__nv_bfloat16>(a, stream)
+                                  : launch_fwd_t<__half>(a, stream);
 }
 
 }  // namespace fa_sm100

@@ -21,6 +21,7 @@ struct FwdArgs {
   float* lse;
   int B, S, H, D;
   int Hkv;  // K/V heads (H % Hkv == 0; H for plain multi-head attention)
+  int dtype = FA_DTYPE_F16;
   float scale;
   int causal;
   int* status;
@@ -46,6 +47,7 @@ struct BwdArgs {
   uint8_t* do_aug;
   int B, S, H, D, S_pad;
   int Hkv;  // K/V heads (H % Hkv == 0); dk, dv are (B, S, Hkv, D)
+  int dtype = FA_DTYPE_F16;
   float scale;
   int causal;
   int* status;
@@ -105,7 +107,7 @@ int bwd_q_rows(int D);
 int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
              const void* out, const float* lse, void* dq, void* dk, void* dv, void* workspace,
              size_t workspace_bytes, int batch, int seqlen, int nheads, int nheads_kv,
-             int head_dim, float sm_scale, int causal, int* status, void* stream);
+             int head_dim, int dtype, float sm_scale, int causal, int* status, void* stream);
 
 // sequence rows are padded to a multiple of this in the backward workspace
 constexpr int kSeqPad = 128;

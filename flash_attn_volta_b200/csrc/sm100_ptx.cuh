@@ -19,6 +19,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace fa_sm100 {
@@ -400,6 +401,52 @@ __device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x2) {
   const float e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
   return f2_pack(e0, e1);
 }
+
+// Element type of the attention tensors (fp16 or bf16): the MMA operand
+// format bits, packing of fp32 pairs (low half = first argument), unpacking,
+// and the bit pattern of 1.0.
+template <typename T>
+struct Elem;
+template <>
+struct Elem<__half> {
+  static constexpr uint32_t kIdescAB = 0;  // A and B format F16 (kind::f16)
+  static constexpr uint32_t kOne = 0x3C00u;
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+  }
+  static __device__ __forceinline__ float2 unpack2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
+  static __device__ __forceinline__ uint16_t bits(float x) {
+    return __half_as_ushort(__float2half_rn(x));
+  }
+  static __device__ __forceinline__ float value(uint16_t b) {
+    return __half2float(__ushort_as_half(b));
+  }
+  static constexpr float kMax = 65504.f;
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr uint32_t kIdescAB = (1u << 7) | (1u << 10);  // A and B format BF16
+  static constexpr uint32_t kOne = 0x3F80u;
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+  }
+  static __device__ __forceinline__ float2 unpack2(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  }
+  static __device__ __forceinline__ uint16_t bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+  static __device__ __forceinline__ float value(uint16_t b) {
+    return __bfloat162float(__ushort_as_bfloat16(b));
+  }
+  static constexpr float kMax = 3.0e38f;
+};
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);

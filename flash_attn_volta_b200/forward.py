@@ -48,10 +48,11 @@ def flash_attn_forward(
     sm_scale: float | None = None,
     return_softmax_lse: bool = False,
 ):
-    """FlashAttention forward on B200: fp16 in/out, fp32 accumulation.
+    """FlashAttention forward on B200: fp16 (or bf16) in/out, fp32 accumulation.
 
     Args:
-        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.  k and v
+        q, k, v: (B, N, H, D) fp16 on CUDA (bf16 also accepted: all three the
+                 same dtype, output in it). D in {16, 32, 64, 128}.  k and v
                  may also have H_kv heads with H % H_kv == 0 (grouped-query or
                  multi-query attention: query head h uses K/V head h // (H // H_kv)).
         causal:  if True apply the top-left lower-triangular mask.
@@ -59,11 +60,12 @@ def flash_attn_forward(
         return_softmax_lse: if True also return the per-row log-sum-exp.
 
     Returns:
-        out: (B, N, H, D) fp16 contiguous; with return_softmax_lse also
+        out: (B, N, H, D) contiguous, q's dtype; with return_softmax_lse also
         lse: (B, H, N) fp32, natural log, +inf for fully masked rows.
     """
     assert q.is_cuda and k.is_cuda and v.is_cuda, "tensors must be on CUDA"
-    assert q.dtype == torch.float16 == k.dtype == v.dtype, "fp16 only"
+    assert q.dtype in (torch.float16, torch.bfloat16) and q.dtype == k.dtype == v.dtype, \
+        "fp16 (or bf16) only, the same for q, k, v"
     Hkv = _kv_heads(q, k, v)
     B, N, H, D = q.shape
     assert D in (16, 32, 64, 128), f"unsupported head_dim {D} (allowed: 16,32,64,128)"
@@ -73,18 +75,19 @@ def flash_attn_forward(
         sm_scale = 1.0 / math.sqrt(D)
 
     q, k, v = _as_kernel_input(q), _as_kernel_input(k), _as_kernel_input(v)
-    out = torch.empty((B, N, H, D), dtype=torch.float16, device=q.device)
+    out = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if return_softmax_lse else None
     if q.numel() != 0:
         lib = _lib.load()
         idx = q.device.index
         with _lib.on_device(idx):
-            rc = lib.fa_sm100_fwd_gqa(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                                      lse.data_ptr() if lse is not None else None,
-                                      B, N, H, Hkv, D, float(sm_scale), 1 if causal else 0,
-                                      _lib.status_ptr(idx), _lib.stream_ptr(idx))
+            rc = lib.fa_sm100_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                     lse.data_ptr() if lse is not None else None,
+                                     B, N, H, Hkv, D, _lib.dtype_code(q.dtype), float(sm_scale),
+                                     1 if causal else 0, _lib.status_ptr(idx),
+                                     _lib.stream_ptr(idx))
         if rc:
-            _lib.check(rc, "fa_sm100_fwd")
+            _lib.check(rc, "fa_sm100_fwd_ex")
         if _lib.debug_sync():
             _lib.check_status(q.device)
     if return_softmax_lse:

@@ -106,9 +106,11 @@ def flash_attention_forward(module, query, key, value, attention_mask, scaling=N
         fn = _original_attention(module, module._fa_orig_impl)
         return fn(module, query, key, value, attention_mask, scaling=scaling, dropout=dropout,
                   **kwargs)
-    q = query.transpose(1, 2).to(torch.float16)
-    k = key.transpose(1, 2).to(torch.float16)
-    v = value.transpose(1, 2).to(torch.float16)
+    # bf16 models stay in bf16 (the kernels take both); anything else runs in fp16
+    dt = torch.bfloat16 if query.dtype == torch.bfloat16 else torch.float16
+    q = query.transpose(1, 2).to(dt)
+    k = key.transpose(1, 2).to(dt)
+    v = value.transpose(1, 2).to(dt)
     sm_scale = float(scaling) if scaling is not None else head_dim ** -0.5
     out = flash_attn(q, k, v, causal=True, sm_scale=sm_scale)
     return out.to(query.dtype), None

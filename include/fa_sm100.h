@@ -34,6 +34,10 @@ extern "C" {
 
 #define FA_SM100_ABI_VERSION 2
 
+/* Element types of the _ex entry points (q, k, v, out, dout, dq, dk, dv). */
+#define FA_DTYPE_F16 0
+#define FA_DTYPE_BF16 1
+
 /* Forward: out = softmax(sm_scale * q k^T [causal mask]) v, and (if lse != NULL)
  * the natural-log log-sum-exp of each query row, +inf for a row with no
  * unmasked key.
@@ -59,21 +63,24 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
                  float sm_scale, int causal, int* status, void* stream);
 
-/* Grouped-query / multi-query attention: k and v (and dk, dv) are
+/* Grouped-query / multi-query attention and bf16: k and v (and dk, dv) are
  * (batch, seqlen, nheads_kv, head_dim) with nheads % nheads_kv == 0; query head
- * h attends to K/V head h / (nheads / nheads_kv).  Otherwise as fa_sm100_fwd /
- * fa_sm100_bwd (same workspace size: fa_sm100_bwd_workspace_bytes with the
- * query head count); dk, dv hold the sums over each K/V head's query heads.
- * No counterpart in the reference: it is multi-head only and its HF patches
- * expand K/V with repeat_kv first (flash_attn_volta/patch_hf.py:187-188). */
-int fa_sm100_fwd_gqa(const void* q, const void* k, const void* v, void* out, float* lse,
-                     int batch, int seqlen, int nheads, int nheads_kv, int head_dim,
-                     float sm_scale, int causal, int* status, void* stream);
-int fa_sm100_bwd_gqa(const void* dout, const void* q, const void* k, const void* v,
-                     const void* out, const float* lse, void* dq, void* dk, void* dv,
-                     void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
-                     int nheads_kv, int head_dim, float sm_scale, int causal, int* status,
-                     void* stream);
+ * h attends to K/V head h / (nheads / nheads_kv).  dtype = FA_DTYPE_F16 or
+ * FA_DTYPE_BF16 for every (batch, seqlen, heads, head_dim) tensor (LSE stays
+ * fp32).  Otherwise as fa_sm100_fwd / fa_sm100_bwd (same workspace size:
+ * fa_sm100_bwd_workspace_bytes with the query head count); dk, dv hold the
+ * sums over each K/V head's query heads.
+ * No counterpart in the reference: it is fp16 and multi-head only
+ * (flash_attn_volta/triton_fa.py:313-317) and its HF patches expand K/V with
+ * repeat_kv first (flash_attn_volta/patch_hf.py:187-188). */
+int fa_sm100_fwd_ex(const void* q, const void* k, const void* v, void* out, float* lse,
+                    int batch, int seqlen, int nheads, int nheads_kv, int head_dim, int dtype,
+                    float sm_scale, int causal, int* status, void* stream);
+int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* v,
+                    const void* out, const float* lse, void* dq, void* dk, void* dv,
+                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
+                    int nheads_kv, int head_dim, int dtype, float sm_scale, int causal,
+                    int* status, void* stream);
 
 /* The three launches fa_sm100_bwd makes, one at a time, on the same arguments:
  * phase 0 = delta and the -LSE/scale, -delta MMA terms, zeroing of the dQ accumulator,

@@ -58,9 +58,9 @@ def load() -> ctypes.CDLL:
                                          _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp,
                                          _vp]
             lib.fa_sm100_bwd.restype = _c_int
-            lib.fa_sm100_fwd_ex.argtypes = [_vp] * 5 + [_c_int] * 6 + [_c_float, _c_int, _vp, _vp]
+            lib.fa_sm100_fwd_ex.argtypes = [_vp] * 5 + [_c_int] * 7 + [_c_float, _c_int, _vp, _vp]
             lib.fa_sm100_fwd_ex.restype = _c_int
-            lib.fa_sm100_bwd_ex.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 6 + [
+            lib.fa_sm100_bwd_ex.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 7 + [
                 _c_float, _c_int, _vp, _vp]
             lib.fa_sm100_bwd_ex.restype = _c_int
             lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes

@@ -31,7 +31,7 @@ def flash_attn_backward(
     Args:
         do: (B, N, H, D) gradient w.r.t. output, q's dtype (fp16 or bf16).
         q, k, v, o: (B, N, H, D) fp16 forward inputs and output (k, v may have
-            H_kv heads, H % H_kv == 0, as in the forward).
+            H_kv heads, H % H_kv == 0, and N_k rows, as in the forward).
         lse: (B, H, N) fp32 log-sum-exp from the forward (+inf on fully masked rows).
         causal, sm_scale: must match the forward call.
 
@@ -55,10 +55,10 @@ def flash_attn_backward(
     do, q, k, v, o = (_as_kernel_input(t) for t in (do, q, k, v, o))
     lse = lse.contiguous()
     dq = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
-    dk = torch.empty((B, N, Hkv, D), dtype=q.dtype, device=q.device)
+    dk = torch.empty((B, k.shape[1], Hkv, D), dtype=q.dtype, device=q.device)
     dv = torch.empty_like(dk)
-    if q.numel() == 0:
-        return dq, dk, dv
+    if q.numel() == 0 or k.shape[1] == 0:
+        return dq.zero_(), dk.zero_(), dv.zero_()
     lib = _lib.load()
     idx = q.device.index
     with _lib.on_device(idx):
@@ -66,7 +66,7 @@ def flash_attn_backward(
         ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
         rc = lib.fa_sm100_bwd_ex(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                  o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                 dv.data_ptr(), ws.data_ptr(), nbytes, B, N, H, Hkv, D,
+                                 dv.data_ptr(), ws.data_ptr(), nbytes, B, N, k.shape[1], H, Hkv, D,
                                  _lib.dtype_code(q.dtype), float(sm_scale), 1 if causal else 0,
                                  _lib.status_ptr(idx), _lib.stream_ptr(idx))
     if rc:

@@ -154,9 +154,10 @@ void fa_sm100_set_debug_flags(int flags) { g_debug_flags.store(flags); }
 
 namespace {
 int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
-             int seqlen, int nheads, int nheads_kv, int head_dim, int dtype, float sm_scale,
-             int causal, int* status, void* stream) {
+             int seqlen, int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+             float sm_scale, int causal, int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  if (!valid_shape(batch, seqlen_k, nheads, head_dim)) return FA_ERR_ARG;
   if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_ARG;
   if (!q || !k || !v || !out || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
@@ -167,9 +168,9 @@ int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse,
   CUtensorMap tq, tk, tv;
   if ((rc = make_bshd_map(&tq, q, batch, seqlen, nheads, head_dim, 128, dtype)) != FA_OK)
     return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen_k, nheads_kv, head_dim, 128, dtype)) != FA_OK)
     return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen_k, nheads_kv, head_dim, 128, dtype)) != FA_OK)
     return rc;
   FwdArgs a;
   a.tm_q = &tq;
@@ -178,7 +179,8 @@ int fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse,
   a.o = out;
   a.lse = lse;
   a.B = batch;
-  a.S = seqlen;
+  a.Sq = seqlen;
+  a.Sk = seqlen_k;
   a.H = nheads;
   a.Hkv = nheads_kv;
   a.dtype = dtype;
@@ -197,15 +199,16 @@ extern "C" {
 int fa_sm100_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
                  int seqlen, int nheads, int head_dim, float sm_scale, int causal, int* status,
                  void* stream) {
-  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16,
-                  sm_scale, causal, status, stream);
+  return fwd_impl(q, k, v, out, lse, batch, seqlen, seqlen, nheads, nheads, head_dim,
+                  FA_DTYPE_F16, sm_scale, causal, status, stream);
 }
 
 int fa_sm100_fwd_ex(const void* q, const void* k, const void* v, void* out, float* lse,
-                    int batch, int seqlen, int nheads, int nheads_kv, int head_dim, int dtype,
-                    float sm_scale, int causal, int* status, void* stream) {
-  return fwd_impl(q, k, v, out, lse, batch, seqlen, nheads, nheads_kv, head_dim, dtype, sm_scale,
-                  causal, status, stream);
+                    int batch, int seqlen_q, int seqlen_k, int nheads, int nheads_kv,
+                    int head_dim, int dtype, float sm_scale, int causal, int* status,
+                    void* stream) {
+  return fwd_impl(q, k, v, out, lse, batch, seqlen_q, seqlen_k, nheads, nheads_kv, head_dim,
+                  dtype, sm_scale, causal, status, stream);
 }
 
 size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim) {
@@ -218,9 +221,10 @@ size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_
 int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k,
                               const void* v, const void* out, const float* lse, void* dq, void* dk,
                               void* dv, void* workspace, size_t workspace_bytes, int batch, int seqlen,
-                              int nheads, int nheads_kv, int head_dim, int dtype, float sm_scale,
-                              int causal, int* status, void* stream) {
+                              int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+                              float sm_scale, int causal, int* status, void* stream) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
+  if (!valid_shape(batch, seqlen_k, nheads, head_dim)) return FA_ERR_ARG;
   if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_ARG;
   const void* ptrs[] = {dout, q, k, v, out, dq, dk, dv};
@@ -238,9 +242,9 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
     return rc;
   if ((rc = make_bshd_map(&tdo, dout, batch, seqlen, nheads, head_dim, qrows, dtype)) != FA_OK)
     return rc;
-  if ((rc = make_bshd_map(&tk, k, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+  if ((rc = make_bshd_map(&tk, k, batch, seqlen_k, nheads_kv, head_dim, 128, dtype)) != FA_OK)
     return rc;
-  if ((rc = make_bshd_map(&tv, v, batch, seqlen, nheads_kv, head_dim, 128, dtype)) != FA_OK)
+  if ((rc = make_bshd_map(&tv, v, batch, seqlen_k, nheads_kv, head_dim, 128, dtype)) != FA_OK)
     return rc;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   BwdArgs a;
@@ -258,7 +262,8 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   a.q_aug = ws + w.q_aug;
   a.do_aug = ws + w.do_aug;
   a.B = batch;
-  a.S = seqlen;
+  a.Sq = seqlen;
+  a.Sk = seqlen_k;
   a.H = nheads;
   a.D = head_dim;
   a.S_pad = (int)round_up((size_t)seqlen, kSeqPad);
@@ -278,17 +283,18 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
                  float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
+                  seqlen, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
                   stream);
 }
 
 int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* v,
                     const void* out, const float* lse, void* dq, void* dk, void* dv,
-                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
-                    int nheads_kv, int head_dim, int dtype, float sm_scale, int causal,
-                    int* status, void* stream) {
+                    void* workspace, size_t workspace_bytes, int batch, int seqlen_q,
+                    int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+                    float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads_kv, head_dim, dtype, sm_scale, causal, status, stream);
+                  seqlen_q, seqlen_k, nheads, nheads_kv, head_dim, dtype, sm_scale, causal, status,
+                  stream);
 }
 
 int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
@@ -297,7 +303,7 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
                        int head_dim, float sm_scale, int causal, int* status, void* stream) {
   if (phase < 0 || phase > 2) return FA_ERR_ARG;
   return bwd_impl(phase, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
-                  seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
+                  seqlen, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
                   stream);
 }
 

@@ -165,7 +165,8 @@ __device__ __forceinline__ uint4 split_row(float x) {
 template <typename T>
 __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const T* __restrict__ o, const T* __restrict__ dout, const float* __restrict__ lse,
-    uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc, int S,
+    uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc,
+    int S /* query rows */,
     int H, int D, int S_pad, float inv_scale) {
   griddep_wait();  // O and LSE come from the forward
   griddep_launch_dependents();
@@ -210,7 +211,8 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
 
 // -------------------------------------------------------------------------- post
 template <typename T>
-__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restrict__ dq, int S,
+__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restrict__ dq,
+                                   int S /* query rows */,
                                    int H, int D, int S_pad, float scale) {
   // one thread per 8 consecutive elements of one (b, s, h) row
   griddep_wait();  // the dQ accumulator comes from the main kernel
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(544, 1)
                        const __grid_constant__ CUtensorMap tm_v,
                        const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
                        float* __restrict__ dq_acc,
-                       T* __restrict__ dk, T* __restrict__ dv, int S, int H, int group,
+                       T* __restrict__ dk, T* __restrict__ dv, int Sq, int Sk, int H, int group,
                        int S_pad,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
@@ -273,15 +275,18 @@ __global__ void __launch_bounds__(544, 1)
   // grouped-query attention (`group` query heads per K/V head) the CTA runs
   // through every query head of its group, so dK / dV sum over the group in
   // tensor memory.
-  const int nkt = (S + C::BN - 1) / C::BN;
+  const int nkt = (Sk + C::BN - 1) / C::BN;
   const int Hkv = H / group;
   int bhk, kt;
   grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nkt), nkt, kHeadGroup, bhk, kt);
   const int b = bhk / Hkv, hk = bhk % Hkv;
   const int kv0 = kt * C::BN;
-  const int ntq = (S + C::BM - 1) / C::BM;
-  const int i0 = causal ? kv0 / C::BM : 0;  // first query tile that sees this key tile
-  const int nq = ntq - i0;                  // query tiles per query head
+  const int ntq = (Sq + C::BM - 1) / C::BM;
+  // causal mask aligned to the bottom-right: query i sees keys j <= i + Sk - Sq
+  const int off = Sk - Sq;
+  // first query tile that sees this key tile
+  const int i0 = causal ? max(0, kv0 - off) / C::BM : 0;
+  const int nq = max(0, ntq - i0);          // query tiles per query head
   const int nit = group * nq;               // iterations: (query head, query tile)
   // iteration it: query head hk * group + it / nq, first row of query tile i0 + it % nq
   // (no division for plain multi-head attention: it sits on the softmax warps' path)
@@ -483,7 +488,7 @@ __global__ void __launch_bounds__(544, 1)
     const int hf = warp >> 2;        // which half of the query columns
     const int r = lq * 32 + lane;    // key row inside the tile == TMEM lane
     const int kv_idx = kv0 + r;
-    const bool kv_ok = kv_idx < S;
+    const bool kv_ok = kv_idx < Sk;
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
     const int c0 = hf * HW;          // first query column of this thread
     bool ok = true;
@@ -502,7 +507,7 @@ __global__ void __launch_bounds__(544, 1)
       // once the previous tile's dV / dK MMAs have read them (PFREE).
 #pragma unroll 1
       // every (query, key) pair of this tile is unmasked
-      const bool full_tile = (kv0 + C::BN <= S) && (!causal || q0 >= kv0 + C::BN - 1);
+      const bool full_tile = (kv0 + C::BN <= Sk) && (!causal || q0 + off >= kv0 + C::BN - 1);
       for (int cc = 0; cc < HW / 32; ++cc) {
         const int cb = c0 + cc * 32;  // first query column of this chunk
         uint32_t sr[32], dr[32];
@@ -542,7 +547,7 @@ __global__ void __launch_bounds__(544, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int ql = cb + e + u;
-              const bool valid = kv_ok && (!causal || (q0 + ql) >= kv_idx);
+              const bool valid = kv_ok && (!causal || (q0 + ql + off) >= kv_idx);
               const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
               p4[u] = pe;
               ds4[u] = pe * __uint_as_float(dr[e + u]);
@@ -585,8 +590,8 @@ __global__ void __launch_bounds__(544, 1)
     constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
     if (ok && hf * EC < D && mbar_wait(bar(C_KVDONE), 0, wc)) {
       tc_fence_after();
-      T* dvrow = dv + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
-      T* dkrow = dk + (((size_t)b * S + kv_idx) * Hkv + hk) * D;
+      T* dvrow = dv + (((size_t)b * Sk + kv_idx) * Hkv + hk) * D;
+      T* dkrow = dk + (((size_t)b * Sk + kv_idx) * Hkv + hk) * D;
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
         const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
@@ -597,6 +602,10 @@ __global__ void __launch_bounds__(544, 1)
           uint32_t v[16];
           tmem_ld16(tmem + lane_base + col + c * 16, v);
           tmem_wait_ld();
+          if (nit == 0) {  // no query row sees this key tile (Sq < Sk): dK = dV = 0
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = 0u;
+          }
           uint4 w0, w1;
           w0.x = Elem<T>::pack2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
           w0.y = Elem<T>::pack2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
@@ -709,11 +718,12 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000);
   if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.Hkv * ((a.S + C::BN - 1) / C::BN));
+  dim3 grid(a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN));
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
       *a.tm_k, *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<T*>(a.dk), static_cast<T*>(a.dv),
-      a.S, a.H, a.H / a.Hkv, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal, a.status,
+      a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal,
+      a.status,
       a.timeout_ns);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
@@ -726,7 +736,7 @@ static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream, int phase) {
     const int rows_per_block = 256 / (a.D / 8);
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
     if (launch_pdl(fa_bwd_pre_kernel<T>, grid, dim3(256), 0, stream, static_cast<const T*>(a.o),
-                   static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.S, a.H,
+                   static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.Sq, a.H,
                    a.D, a.S_pad, 1.0f / a.scale) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
@@ -741,10 +751,10 @@ static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream, int phase) {
   if (rc != FA_OK) return rc;
   if (phase < 0 || phase == 2) {
     const int per_row = a.D / 8;
-    const size_t n = (size_t)a.S * per_row;
+    const size_t n = (size_t)a.Sq * per_row;
     dim3 grid((unsigned)((n + 255) / 256), a.B * a.H);
     if (launch_pdl(fa_bwd_post_kernel<T>, grid, dim3(256), 0, stream, a.dq_acc,
-                   static_cast<T*>(a.dq), a.S, a.H, a.D, a.S_pad, a.scale) != cudaSuccess)
+                   static_cast<T*>(a.dq), a.Sq, a.H, a.D, a.S_pad, a.scale) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   return FA_OK;

@@ -34,6 +34,9 @@
 // Semantics kept from the reference: top-left causal mask (column > row is
 // masked, triton_fa.py:124-126), columns >= S masked (:123), LSE = m + ln(l)
 // and +inf for a row with l == 0 (:152-159), rows >= S not stored (:149-150).
+// Beyond the reference: Sq != Sk (query rows against a key sequence of another
+// length) with the causal mask aligned to the bottom-right, query i seeing keys
+// j <= i + Sk - Sq (identical to the above when Sq == Sk).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -117,7 +120,8 @@ template <int D, typename T>
 __global__ void __launch_bounds__(640, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
-                  float* __restrict__ lse, int S, int H, int group, float scale_log2, int causal,
+                  float* __restrict__ lse, int Sq, int Sk, int H, int group, float scale_log2,
+                  int causal,
                   int* status, unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -140,15 +144,18 @@ __global__ void __launch_bounds__(640, 1)
   }
   // 1-D grid over (head group, query block rank, head): longest blocks first
   // inside each group of heads, K/V of only a few heads live at once (L2 reuse)
-  const int nblk = (S + C::BM - 1) / C::BM;
+  const int nblk = (Sq + C::BM - 1) / C::BM;
   int bh, rank;
   grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nblk), nblk, kHeadGroup, bh, rank);
   const int qt = causal ? (nblk - 1 - rank) : rank;
   const int b = bh / H, h = bh % H;
   const int hk = h / group;  // K/V head (grouped-query attention: `group` query heads per K/V head)
   const int q0 = qt * C::BM;
-  const int nkv_all = (S + C::BN - 1) / C::BN;
-  const int nkv = causal ? min(nkv_all, (q0 + C::BM + C::BN - 1) / C::BN) : nkv_all;
+  // causal mask aligned to the bottom-right: query i sees keys j <= i + Sk - Sq
+  // (the top-left mask of square attention when Sq == Sk)
+  const int off = Sk - Sq;
+  const int nkv_all = (Sk + C::BN - 1) / C::BN;
+  const int nkv = causal ? max(0, min(nkv_all, (q0 + C::BM + off + C::BN - 1) / C::BN)) : nkv_all;
 
   WaitCtx wc{abort_flag, status, timeout_ns};
 
@@ -319,9 +326,9 @@ __global__ void __launch_bounds__(640, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_SFREE + sb));
       const int kv0 = j * C::BN + cq * QC;
-      const bool need_mask = (kv0 + QC > S) || (causal && kv0 + QC - 1 > q0);
+      const bool need_mask = (kv0 + QC > Sk) || (causal && kv0 + QC - 1 > q0 + off);
       if (need_mask) {
-        const int lim = min(S - kv0, causal ? (q_idx - kv0 + 1) : QC);
+        const int lim = min(Sk - kv0, causal ? (q_idx + off - kv0 + 1) : QC);
 #pragma unroll
         for (int c = 0; c < QC; ++c)
           if (c >= lim) sv[c] = NEG_INF;
@@ -404,6 +411,10 @@ __global__ void __launch_bounds__(640, 1)
     }
     // ------------------------------------------------------------ epilogue
     if (ok && nkv > 0) {
+      // A row that saw no finite score (every key masked: only when Sq > Sk)
+      // keeps l = 0, i.e. O = 0 and LSE = +inf; the FMA-pipe exp2 returns 2^-125,
+      // not 0, for masked scores, which only rows with a finite score may absorb.
+      if (m_run == NEG_INF) l_run = 0.f;
       // the full row sum: the four column quarters' shares
       float* xs = xch + (nkv & 1) * 512;
       xs[cq * 128 + r] = l_run;
@@ -420,8 +431,8 @@ __global__ void __launch_bounds__(640, 1)
         mbar_wait(bar(B_PFREE + ((nkv - 1) & 1)), (uint32_t)((nkv - 1) >> 1) & 1u, wc)) {
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-      const bool row_ok = q_idx < S;
-      T* orow = out + (((size_t)b * S + q_idx) * H + h) * D + cq * EC;
+      const bool row_ok = q_idx < Sq;
+      T* orow = out + (((size_t)b * Sq + q_idx) * H + h) * D + cq * EC;
       if (o_cols) {
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
@@ -445,9 +456,16 @@ __global__ void __launch_bounds__(640, 1)
       }
       if (lse != nullptr && row_ok && cq == 0) {
         const float m_safe = (m_run == NEG_INF) ? 0.f : m_run;
-        lse[(size_t)bh * S + q_idx] =
+        lse[(size_t)bh * Sq + q_idx] =
             l_run > 0.f ? (m_safe + lg2(l_run)) * 0.69314718055994530942f : __int_as_float(0x7f800000);
       }
+    }
+    if (nkv == 0 && q_idx < Sq) {
+      // every key is masked for these rows (only when Sq > Sk): O = 0, LSE = +inf
+      T* orow = out + (((size_t)b * Sq + q_idx) * H + h) * D + cq * EC;
+      if (o_cols)
+        for (int c = 0; c < EC; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+      if (lse != nullptr && cq == 0) lse[(size_t)bh * Sq + q_idx] = __int_as_float(0x7f800000);
     }
   }
 
@@ -469,10 +487,11 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   constexpr int tag = D + (std::is_same<T, __half>::value ? 0 : 1000);
   if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_fwd_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.H * ((a.S + C::BM - 1) / C::BM));
+  dim3 grid(a.B * a.H * ((a.Sq + C::BM - 1) / C::BM));
   const cudaError_t e = launch_pdl(fa_fwd_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream,
                                    *a.tm_q, *a.tm_k, *a.tm_v, static_cast<T*>(a.o), a.lse,
-                                   a.S, a.H, a.H / a.Hkv, a.scale * 1.4426950408889634f, a.causal,
+                                   a.Sq, a.Sk, a.H, a.H / a.Hkv, a.scale * 1.4426950408889634f,
+                                   a.causal,
                                    a.status, a.timeout_ns, a.debug_flags);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }

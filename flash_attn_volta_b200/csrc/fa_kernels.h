@@ -19,7 +19,8 @@ struct FwdArgs {
   const CUtensorMap* tm_v;  // box rows: 128
   void* o;
   float* lse;
-  int B, S, H, D;
+  int B, Sq, H, D;
+  int Sk;   // key / value rows (Sq for square attention)
   int Hkv;  // K/V heads (H % Hkv == 0; H for plain multi-head attention)
   int dtype = FA_DTYPE_F16;
   float scale;
@@ -45,7 +46,8 @@ struct BwdArgs {
   // extra K step of S^T (-LSE/scale) and of dP^T (-delta) as fp16 hi/lo pairs
   uint8_t* q_aug;
   uint8_t* do_aug;
-  int B, S, H, D, S_pad;
+  int B, Sq, H, D, S_pad;  // S_pad: Sq rounded up to kSeqPad
+  int Sk;                  // key / value rows
   int Hkv;  // K/V heads (H % Hkv == 0); dk, dv are (B, S, Hkv, D)
   int dtype = FA_DTYPE_F16;
   float scale;
@@ -106,8 +108,9 @@ int bwd_q_rows(int D);
 // workspace (phase as in launch_bwd).  Shared by the C ABI entry points.
 int bwd_impl(int phase, const void* dout, const void* q, const void* k, const void* v,
              const void* out, const float* lse, void* dq, void* dk, void* dv, void* workspace,
-             size_t workspace_bytes, int batch, int seqlen, int nheads, int nheads_kv,
-             int head_dim, int dtype, float sm_scale, int causal, int* status, void* stream);
+             size_t workspace_bytes, int batch, int seqlen, int seqlen_k, int nheads,
+             int nheads_kv, int head_dim, int dtype, float sm_scale, int causal, int* status,
+             void* stream);
 
 // sequence rows are padded to a multiple of this in the backward workspace
 constexpr int kSeqPad = 128;

@@ -27,10 +27,11 @@ def _as_kernel_input(t: torch.Tensor) -> torch.Tensor:
 
 def _kv_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> int:
     """K/V head count: q's (multi-head) or a divisor of it (grouped-query /
-    multi-query attention: k and v are (B, N, H_kv, D)).  Anything else raises
-    the reference's AssertionError."""
-    ok = (k.shape == v.shape and q.dim() == 4 and k.dim() == 4 and q.shape[:2] == k.shape[:2]
-          and q.shape[3] == k.shape[3] and k.shape[2] > 0 and q.shape[2] % k.shape[2] == 0)
+    multi-query attention: k and v are (B, N_k, H_kv, D), N_k may differ from
+    q's N).  Anything else raises the reference's AssertionError."""
+    ok = (k.shape == v.shape and q.dim() == 4 and k.dim() == 4 and q.shape[0] == k.shape[0]
+          and q.shape[3] == k.shape[3] and k.shape[2] > 0
+          and q.shape[2] % k.shape[2] == 0)
     assert ok, f"qkv shape mismatch {q.shape} {k.shape} {v.shape}"
     return k.shape[2]
 
@@ -54,8 +55,11 @@ def flash_attn_forward(
         q, k, v: (B, N, H, D) fp16 on CUDA (bf16 also accepted: all three the
                  same dtype, output in it). D in {16, 32, 64, 128}.  k and v
                  may also have H_kv heads with H % H_kv == 0 (grouped-query or
-                 multi-query attention: query head h uses K/V head h // (H // H_kv)).
-        causal:  if True apply the top-left lower-triangular mask.
+                 multi-query attention: query head h uses K/V head h // (H // H_kv)),
+                 and N_k rows instead of N (KV-cache prefill and the like).
+        causal:  if True apply the top-left lower-triangular mask (for N_k != N
+                 aligned to the bottom-right: query i sees keys j <= i + N_k - N;
+                 a query row that sees no key gets out 0 and lse +inf).
         sm_scale: softmax scale (default 1/sqrt(D)).
         return_softmax_lse: if True also return the per-row log-sum-exp.
 
@@ -77,13 +81,19 @@ def flash_attn_forward(
     q, k, v = _as_kernel_input(q), _as_kernel_input(k), _as_kernel_input(v)
     out = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if return_softmax_lse else None
-    if q.numel() != 0:
+    if q.numel() != 0 and k.shape[1] == 0:
+        # no keys at all: every query row is fully masked (O = 0, LSE = +inf)
+        out.zero_()
+        if lse is not None:
+            lse.fill_(float("inf"))
+    elif q.numel() != 0:
         lib = _lib.load()
         idx = q.device.index
         with _lib.on_device(idx):
             rc = lib.fa_sm100_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                      lse.data_ptr() if lse is not None else None,
-                                     B, N, H, Hkv, D, _lib.dtype_code(q.dtype), float(sm_scale),
+                                     B, N, k.shape[1], H, Hkv, D, _lib.dtype_code(q.dtype),
+                                     float(sm_scale),
                                      1 if causal else 0, _lib.status_ptr(idx),
                                      _lib.stream_ptr(idx))
         if rc:

@@ -63,24 +63,29 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  size_t workspace_bytes, int batch, int seqlen, int nheads, int head_dim,
                  float sm_scale, int causal, int* status, void* stream);
 
-/* Grouped-query / multi-query attention and bf16: k and v (and dk, dv) are
- * (batch, seqlen, nheads_kv, head_dim) with nheads % nheads_kv == 0; query head
- * h attends to K/V head h / (nheads / nheads_kv).  dtype = FA_DTYPE_F16 or
- * FA_DTYPE_BF16 for every (batch, seqlen, heads, head_dim) tensor (LSE stays
- * fp32).  Otherwise as fa_sm100_fwd / fa_sm100_bwd (same workspace size:
- * fa_sm100_bwd_workspace_bytes with the query head count); dk, dv hold the
- * sums over each K/V head's query heads.
- * No counterpart in the reference: it is fp16 and multi-head only
+/* Extended forward / backward: grouped-query attention, bf16 and Sq != Sk.
+ * q, out, dout, dq are (batch, seqlen_q, nheads, head_dim); k, v, dk, dv are
+ * (batch, seqlen_k, nheads_kv, head_dim) with nheads % nheads_kv == 0, query
+ * head h attending to K/V head h / (nheads / nheads_kv); lse is
+ * (batch, nheads, seqlen_q) fp32.  dtype = FA_DTYPE_F16 or FA_DTYPE_BF16 for
+ * every (batch, seq, heads, head_dim) tensor.  With seqlen_q != seqlen_k the
+ * causal mask is aligned to the bottom-right: query i sees keys
+ * j <= i + seqlen_k - seqlen_q (a row that sees no key gets out = 0,
+ * lse = +inf).  Otherwise as fa_sm100_fwd / fa_sm100_bwd; the workspace is
+ * fa_sm100_bwd_workspace_bytes(batch, seqlen_q, nheads, head_dim); dk, dv hold
+ * the sums over each K/V head's query heads.
+ * No counterpart in the reference: it is fp16, multi-head and square only
  * (flash_attn_volta/triton_fa.py:313-317) and its HF patches expand K/V with
  * repeat_kv first (flash_attn_volta/patch_hf.py:187-188). */
 int fa_sm100_fwd_ex(const void* q, const void* k, const void* v, void* out, float* lse,
-                    int batch, int seqlen, int nheads, int nheads_kv, int head_dim, int dtype,
-                    float sm_scale, int causal, int* status, void* stream);
+                    int batch, int seqlen_q, int seqlen_k, int nheads, int nheads_kv,
+                    int head_dim, int dtype, float sm_scale, int causal, int* status,
+                    void* stream);
 int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* v,
                     const void* out, const float* lse, void* dq, void* dk, void* dv,
-                    void* workspace, size_t workspace_bytes, int batch, int seqlen, int nheads,
-                    int nheads_kv, int head_dim, int dtype, float sm_scale, int causal,
-                    int* status, void* stream);
+                    void* workspace, size_t workspace_bytes, int batch, int seqlen_q,
+                    int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+                    float sm_scale, int causal, int* status, void* stream);
 
 /* The three launches fa_sm100_bwd makes, one at a time, on the same arguments:
  * phase 0 = delta and the -LSE/scale, -delta MMA terms, zeroing of the dQ accumulator,

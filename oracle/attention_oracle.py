@@ -44,19 +44,24 @@ __all__ = [
 ]
 
 
-def _scores(q, k, causal, scale, dtype):
-    """(B,S,H,D) inputs -> (B,H,Sq,Sk) scaled, masked scores (ref.py:22-32)."""
+def _scores(q, k, causal, scale, dtype, causal_offset=0):
+    """(B,S,H,D) inputs -> (B,H,Sq,Sk) scaled, masked scores (ref.py:22-32).
+
+    The causal mask keeps key j for query i when j <= i + causal_offset; the
+    reference's square attention is causal_offset = 0 (top-left).  The kernels'
+    Sq != Sk extension uses causal_offset = Sk - Sq (bottom-right alignment)."""
     qh = q.permute(0, 2, 1, 3).to(dtype)
     kh = k.permute(0, 2, 1, 3).to(dtype)
     s = torch.einsum("bhnd,bhmd->bhnm", qh, kh) * scale
     if causal:
         n, m = s.shape[-2], s.shape[-1]
-        mask = torch.triu(torch.full((n, m), float("-inf"), dtype=dtype), diagonal=1)
+        mask = torch.triu(torch.full((n, m), float("-inf"), dtype=dtype),
+                          diagonal=1 + causal_offset)
         s = s + mask
     return s
 
 
-def attention_fwd(q, k, v, causal=False, scale=None, dtype=torch.float32):
+def attention_fwd(q, k, v, causal=False, scale=None, dtype=torch.float32, *, causal_offset=0):
     """Exact forward. Returns (o (B,S,H,D) in `dtype`, lse (B,H,S) in `dtype`).
 
     Follows ref.py:9-36; the LSE convention follows triton_fa.py:152-159.
@@ -64,7 +69,7 @@ def attention_fwd(q, k, v, causal=False, scale=None, dtype=torch.float32):
     D = q.shape[-1]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    s = _scores(q, k, causal, scale, dtype)
+    s = _scores(q, k, causal, scale, dtype, causal_offset)
     lse = torch.logsumexp(s, dim=-1)
     # a row with every key masked: l == 0 -> the reference stores +inf
     lse = torch.where(torch.isneginf(lse), torch.full_like(lse, float("inf")), lse)
@@ -75,7 +80,8 @@ def attention_fwd(q, k, v, causal=False, scale=None, dtype=torch.float32):
     return o, lse
 
 
-def attention_bwd(do, q, k, v, causal=False, scale=None, dtype=torch.float64):
+def attention_bwd(do, q, k, v, causal=False, scale=None, dtype=torch.float64, *,
+                  causal_offset=0):
     """Exact backward. Returns (dq, dk, dv), each (B,S,H,D) in `dtype`.
 
     Restates triton_fa_bwd.py's algorithm (see module docstring) without tiling
@@ -84,7 +90,7 @@ def attention_bwd(do, q, k, v, causal=False, scale=None, dtype=torch.float64):
     D = q.shape[-1]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    s = _scores(q, k, causal, scale, dtype)
+    s = _scores(q, k, causal, scale, dtype, causal_offset)
     p = torch.nan_to_num(torch.softmax(s, dim=-1), nan=0.0)
     vh = v.permute(0, 2, 1, 3).to(dtype)
     qh = q.permute(0, 2, 1, 3).to(dtype)

@@ -83,15 +83,17 @@ def test_ex_head_count_and_dtype_checks():
     """fa_sm100_*_ex reject a K/V head count that does not divide the query heads
     and an unknown element type before touching the device."""
     lib = _lib.load()
-    args_f = (16, 16, 16, 16, None, 1, 64, 8, 3, 64, _lib.DTYPE_F16, 0.125, 1, None, None)
+    f16, bf16 = _lib.DTYPE_F16, _lib.DTYPE_BF16
+    args_f = (16, 16, 16, 16, None, 1, 64, 64, 8, 3, 64, f16, 0.125, 1, None, None)
     assert lib.fa_sm100_fwd_ex(*args_f) == _lib.FA_ERR_ARG
-    args_f0 = (16, 16, 16, 16, None, 1, 64, 8, 0, 64, _lib.DTYPE_BF16, 0.125, 1, None, None)
+    args_f0 = (16, 16, 16, 16, None, 1, 64, 64, 8, 0, 64, bf16, 0.125, 1, None, None)
     assert lib.fa_sm100_fwd_ex(*args_f0) == _lib.FA_ERR_ARG
-    args_dt = (16, 16, 16, 16, None, 1, 64, 8, 2, 64, 7, 0.125, 1, None, None)
+    args_dt = (16, 16, 16, 16, None, 1, 64, 64, 8, 2, 64, 7, 0.125, 1, None, None)
     assert lib.fa_sm100_fwd_ex(*args_dt) == _lib.FA_ERR_ARG
+    args_sk = (16, 16, 16, 16, None, 1, 64, 0, 8, 2, 64, f16, 0.125, 1, None, None)
+    assert lib.fa_sm100_fwd_ex(*args_sk) == _lib.FA_ERR_ARG  # no keys
     n = lib.fa_sm100_bwd_workspace_bytes(1, 64, 8, 64)
-    rc = lib.fa_sm100_bwd_ex(*([256] * 9), 256, n, 1, 64, 8, 3, 64, _lib.DTYPE_F16, 0.125, 1,
-                             None, None)
+    rc = lib.fa_sm100_bwd_ex(*([256] * 9), 256, n, 1, 64, 64, 8, 3, 64, f16, 0.125, 1, None, None)
     assert rc == _lib.FA_ERR_ARG
-    rc = lib.fa_sm100_bwd_ex(*([256] * 9), 256, n, 1, 64, 8, 2, 64, 9, 0.125, 1, None, None)
+    rc = lib.fa_sm100_bwd_ex(*([256] * 9), 256, n, 1, 64, 64, 8, 2, 64, 9, 0.125, 1, None, None)
     assert rc == _lib.FA_ERR_ARG

@@ -661,9 +661,24 @@ def run_ring(args):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
+    # count this library's launches in the timed steps: one forward kernel per
+    # forward block, three (prep, main, dQ conversion) per backward block
+    counts = [0]
+    fwd0, bwd0 = ring.block_fwd, ring.block_bwd
+
+    def fwd_counted(*a):
+        counts[0] += 1
+        return fwd0(*a)
+
+    def bwd_counted(*a):
+        counts[0] += 3
+        return bwd0(*a)
+
+    ring.block_fwd, ring.block_bwd = fwd_counted, bwd_counted
     if world > 1:
         dist.barrier()
     ms = time_steps(step, args.steps, torch.cuda.current_stream(dev))
+    ring.block_fwd, ring.block_bwd = fwd0, bwd0
     if world > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -682,7 +697,7 @@ def run_ring(args):
                        "l2": "inputs (1 GiB per tensor) larger than L2"},
             "pct_of_peak": {"value": value / (world * peak_sus), "peak_tflops": world * peak_sus,
                             "kind": f"{peak_kind} bf16 sustained x n_gpus"},
-            "gpu_launches": None,
+            "gpu_launches": counts[0],
         }), flush=True)
     if world > 1:
         dist.barrier()

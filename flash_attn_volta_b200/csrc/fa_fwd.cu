@@ -21,8 +21,8 @@
 //              in four on the FMA pipe), writes P to tensor memory and rescales
 //              its share of O when the running max grew by more than 2^8
 //              (lazy rescale); epilogue O/l and LSE.
-//   warp 16    TMA producer: Q once, then K tiles through their ring.
-//   warp 19    TMA producer: V tiles through their ring.
+//   warp 16    TMA producers: lane 0 Q once, then K tiles through their ring;
+//              lane 1 V tiles through their ring.
 //   warp 17    S issuer:  S_b = Q K_j^T (b = j % 2) once the softmax warps
 //              have read S_b of tile j-2.
 //   warp 18    PV issuer: O += P_b V_j (P_b as the tensor-memory A operand)
@@ -94,7 +94,7 @@ struct FwdCfg {
   static constexpr int XCH_BYTES = 2 * 4 * 128 * 4;    // [parity][column quarter][row]
   static constexpr int SMEM = OFF_XCH + XCH_BYTES + 1024;  // + alignment slack
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 640;
+  static constexpr int THREADS = 608;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // S_b: +128 b, P_b: +64 b
 };
@@ -117,7 +117,7 @@ enum FwdBar {
 };
 
 template <int D, typename T>
-__global__ void __launch_bounds__(640, 1)
+__global__ void __launch_bounds__(608, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
                   float* __restrict__ lse, int Sq, int Sk, int H, int group, float scale_log2,
@@ -183,10 +183,12 @@ __global__ void __launch_bounds__(640, 1)
   griddep_launch_dependents();
 
   if (warp == 16) {
-    // ------------------------------------------------------------ TMA producer: Q, K
-    // K runs ahead on its own ring: were K and V issued by one thread, each K
-    // load would queue behind a V slot that frees only when O += P V of two
-    // tiles back completes, about one load latency before S needs that K.
+    // ------------------------------------------------------------ TMA producers
+    // Lane 0: Q, then the K ring; lane 1: the V ring.  K runs ahead on its own
+    // thread: were K and V issued by one thread, each K load would queue behind
+    // a V slot that frees only when O += P V of two tiles back completes, about
+    // one load latency before S needs that K.  (Two lanes of one warp, not two
+    // warps: the softmax warps need the registers.)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -212,10 +214,7 @@ __global__ void __launch_bounds__(640, 1)
         for (int j = max(0, loaded - C::NSTK); j < loaded; ++j)
           mbar_wait_drain(bar(B_KFULL + j % C::NSTK), (uint32_t)(j / C::NSTK) & 1u, timeout_ns);
       }
-    }
-  } else if (warp == 19) {
-    // ------------------------------------------------------------ TMA producer: V
-    if (lane == 0) {
+    } else if (lane == 1) {
       tma_prefetch_desc(&tm_v);
       int loaded = 0;
       for (int j = 0; j < nkv; ++j) {
@@ -313,14 +312,18 @@ __global__ void __launch_bounds__(640, 1)
     float m_run = NEG_INF;  // running max, already multiplied by scale*log2(e)
     float l_run = 0.f;      // this warp's share of the row sum
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    // stage(j): S of step j into registers (its buffer released at once), masked,
+    // and this quarter's row max posted to the exchange.  The loop stages step
+    // j + 1 right after step j's P values are computed, so the load and the four
+    // warps' exchange overlap step j's P store instead of stalling all of them
+    // together at the top of the next step.
+    auto stage = [&](int j, float (&dst)[QC]) -> bool {
       const int sb = j & 1;
-      if (!mbar_wait(bar(B_SFULL + sb), (uint32_t)(j >> 1) & 1u, wc)) { ok = false; break; }
+      if (!mbar_wait(bar(B_SFULL + sb), (uint32_t)(j >> 1) & 1u, wc)) return false;
       if (threadIdx.x == 0) FTRACE(8, j);
       tc_fence_after();
-      float sv[QC];
       tmem_ld32(tmem + lane_base + C::COL_S + sb * 128 + cq * QC,
-                *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                *reinterpret_cast<uint32_t(*)[32]>(&dst[0]));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -331,19 +334,29 @@ __global__ void __launch_bounds__(640, 1)
         const int lim = min(Sk - kv0, causal ? (q_idx + off - kv0 + 1) : QC);
 #pragma unroll
         for (int c = 0; c < QC; ++c)
-          if (c >= lim) sv[c] = NEG_INF;
+          if (c >= lim) dst[c] = NEG_INF;
       }
-      float mt = fmax3(sv[0], sv[1], sv[2]);
+      float mx[4];
 #pragma unroll
-      for (int c = 3; c < QC - 1; c += 2) mt = fmax3(mt, sv[c], sv[c + 1]);
-      mt = fmaxf(mt, sv[QC - 1]);
-      // row max over the four column quarters
+      for (int u = 0; u < 4; ++u) mx[u] = fmaxf(dst[u], dst[4 + u]);
+#pragma unroll
+      for (int c = 8; c < QC; c += 8)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx[u] = fmax3(mx[u], dst[c + u], dst[c + 4 + u]);
       float* xs = xch + (j & 1) * 512;
-      xs[cq * 128 + r] = mt;
+      xs[cq * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
+      return true;
+    };
+    float sv[QC];
+    if (nkv > 0 && !stage(0, sv)) ok = false;
+    for (int j = 0; ok && j < nkv; ++j) {
+      const int sb = j & 1;
+      // row max over the four column quarters (posted one iteration earlier)
       if (!mbar_wait(xbar, (uint32_t)j & 1u, wc)) { ok = false; break; }
-      mt = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
+      const float* xs = xch + (j & 1) * 512;
+      const float mt = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
       const float m_new = fmaxf(m_run, mt * scale_log2);
       // Lazy rescale: keep the old reference max unless the row max grew by > 8
       // (a factor 256 in P), or this is the first finite max of the row.
@@ -378,6 +391,8 @@ __global__ void __launch_bounds__(640, 1)
       f2_unpack(sum2, lsum0, lsum1);
       l_run = l_run * alpha + (lsum0 + lsum1);
       if (threadIdx.x == 0) FTRACE(9, j);
+      // this step's scores are dead: stage the next step into their registers
+      if (j + 1 < nkv && !stage(j + 1, sv)) { ok = false; break; }
       // P_b is free once O += P_b V of tile j-2 has read it
       if (j >= 2 && !mbar_wait(bar(B_PFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)) {
         ok = false;

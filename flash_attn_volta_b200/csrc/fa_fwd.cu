@@ -7,7 +7,11 @@
 // (B, S, H, D) fp16 tensors (row stride H*D), every head_dim in {16,32,64,128}
 // runs natively (no zero padding), and O is written in (B, S, H, D).
 //
-// One CTA = one 128-row query tile of one (batch, head).  Tensor memory (512
+// Persistent: one CTA per SM walks a list of 128-row query tiles of the
+// (batch, head) pairs (round r takes tile r * grid + CTA, in reverse CTA order
+// on odd rounds, over a longest-first order), so the set-up is paid once per SM
+// and the next tile's Q load and first S = Q K^T overlap this tile's last
+// softmax step and its epilogue.  Tensor memory (512
 // columns): S0 [0,128), S1 [128,256) — S = Q K_j^T double-buffered; P0
 // [256,320), P1 [320,384) — P (fp16 pairs) double-buffered; O [384, 384+D).
 // Because P has its own columns, nothing in the tensor-core stream waits for
@@ -21,12 +25,16 @@
 //              in four on the FMA pipe), writes P to tensor memory and rescales
 //              its share of O when the running max grew by more than 2^8
 //              (lazy rescale); epilogue O/l and LSE.
-//   warp 16    TMA producers: lane 0 Q once, then K tiles through their ring;
+//   warp 16    TMA producers: lane 0 Q of each tile (once the previous tile's
+//              last S MMA has read its Q), then K tiles through their ring;
 //              lane 1 V tiles through their ring.
 //   warp 17    S issuer:  S_b = Q K_j^T (b = j % 2) once the softmax warps
 //              have read S_b of tile j-2.
 //   warp 18    PV issuer: O += P_b V_j (P_b as the tensor-memory A operand)
-//              once the softmax warps have written P_b.
+//              once the softmax warps have written P_b; a tile's first PV
+//              (which overwrites O) waits until the previous tile's epilogue
+//              has read O.
+// Barrier phases count steps (and tiles) over the CTA's whole tile list.
 // One thread issues about one tcgen05.mma per ~55 clk, close to the 64 clk an
 // M128 x N128 x K16 MMA takes, so the S and PV chains get a thread each and
 // interleave on the tensor core.
@@ -113,15 +121,21 @@ enum FwdBar {
   B_ODONE = 25,   // every O += P V (waited only where at most one phase is pending)
   B_XCHG = 26,    // +row quarter, 4 arrivals
   B_DRAIN = 30,   // 2 arrivals: each issuer's last commit
-  B_COUNT = 31
+  B_QEMPTY = 31,  // a tile's last S MMA has read Q
+  B_OFREE = 32,   // 16 arrivals: the epilogue has read O
+  B_COUNT = 33
 };
+
+// Heads per window of the forward's tile list (K/V of 16 heads at S = 8192,
+// D = 128: 64 MiB, within L2).
+constexpr int kFwdHeadWindow = 16;
 
 template <int D, typename T>
 __global__ void __launch_bounds__(608, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
-                  float* __restrict__ lse, int Sq, int Sk, int H, int group, float scale_log2,
-                  int causal,
+                  float* __restrict__ lse, int Sq, int Sk, int H, int group, int ntiles,
+                  float scale_log2, int causal,
                   int* status, unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -142,27 +156,44 @@ __global__ void __launch_bounds__(608, 1)
     if (blockIdx.x < 8192) g_fcta[blockIdx.x][0] = smid;
 #endif
   }
-  // 1-D grid over (head group, query block rank, head): longest blocks first
-  // inside each group of heads, K/V of only a few heads live at once (L2 reuse)
+  // Tile list: ntiles tiles in the order (window of kFwdHeadWindow heads, query
+  // block rank, head), longest blocks first inside each window so that K/V of
+  // only a few heads live at once (L2 reuse) while the tiles dealt out in one
+  // round have similar lengths.  Round t gives this CTA tile t * grid + pos,
+  // pos = blockIdx.x on even rounds and its mirror on odd ones (the CTA with
+  // the longest tile of one round gets the shortest of the next).
   const int nblk = (Sq + C::BM - 1) / C::BM;
-  int bh, rank;
-  grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nblk), nblk, kHeadGroup, bh, rank);
-  const int qt = causal ? (nblk - 1 - rank) : rank;
-  const int b = bh / H, h = bh % H;
-  const int hk = h / group;  // K/V head (grouped-query attention: `group` query heads per K/V head)
-  const int q0 = qt * C::BM;
+  const int rounds = (ntiles + (int)gridDim.x - 1) / (int)gridDim.x;
   // causal mask aligned to the bottom-right: query i sees keys j <= i + Sk - Sq
   // (the top-left mask of square attention when Sq == Sk)
   const int off = Sk - Sq;
   const int nkv_all = (Sk + C::BN - 1) / C::BN;
-  const int nkv = causal ? max(0, min(nkv_all, (q0 + C::BM + off + C::BN - 1) / C::BN)) : nkv_all;
+  struct Tile {
+    int b, h, hk, bh, q0, nkv;
+  };
+  auto tile_at = [&](int t, Tile& tl) -> bool {
+    const int pos = (t & 1) ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int L = t * (int)gridDim.x + pos;
+    if (L >= ntiles) return false;
+    int bh, rank;
+    grid_to_tile(L, ntiles / nblk, nblk, kFwdHeadWindow, bh, rank);
+    const int qt = causal ? (nblk - 1 - rank) : rank;
+    tl.bh = bh;
+    tl.b = bh / H;
+    tl.h = bh % H;
+    tl.hk = tl.h / group;  // K/V head (grouped-query attention: `group` query heads per K/V head)
+    tl.q0 = qt * C::BM;
+    tl.nkv = causal ? max(0, min(nkv_all, (tl.q0 + C::BM + off + C::BN - 1) / C::BN)) : nkv_all;
+    return true;
+  };
 
   WaitCtx wc{abort_flag, status, timeout_ns};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < B_COUNT; ++i) {
       uint32_t cnt = 1;
-      if (i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1) cnt = 16;
+      if (i == B_SFREE || i == B_SFREE + 1 || i == B_PFULL || i == B_PFULL + 1 || i == B_OFREE)
+        cnt = 16;
       if (i >= B_XCHG && i < B_XCHG + 4) cnt = 4;
       if (i == B_DRAIN) cnt = 2;
       mbar_init(bar(i), cnt);
@@ -192,49 +223,69 @@ __global__ void __launch_bounds__(608, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      mbar_arrive_expect_tx(bar(B_QFULL), C::Q_BYTES);
-      for (int a = 0; a < C::NAT; ++a)
-        tma_load_4d(sbase + C::OFF_Q + a * C::BM * C::SWB, &tm_q, bar(B_QFULL), a * C::AE, q0, h,
-                    b);
-      int loaded = 0;
-      for (int j = 0; j < nkv; ++j) {
-        const int sk = j % C::NSTK;
-        if (j >= C::NSTK &&
-            !mbar_wait(bar(B_KEMPTY + sk), (uint32_t)(j / C::NSTK - 1) & 1u, wc))
-          break;
-        mbar_arrive_expect_tx(bar(B_KFULL + sk), C::KV_BYTES);
+      int loaded = 0;  // K loads issued (steps over the whole tile list)
+      int nq = 0;      // Q loads issued
+      int gs = 0;      // steps of the earlier tiles
+      bool ok = true;
+      for (int t = 0; ok && t < rounds; ++t) {
+        Tile tl;
+        if (!tile_at(t, tl) || tl.nkv == 0) continue;
+        if (nq > 0 && !mbar_wait(bar(B_QEMPTY), (uint32_t)(nq - 1) & 1u, wc)) break;
+        mbar_arrive_expect_tx(bar(B_QFULL), C::Q_BYTES);
         for (int a = 0; a < C::NAT; ++a)
-          tma_load_4d(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
-                      bar(B_KFULL + sk), a * C::AE, j * C::BN, hk, b);
-        loaded = j + 1;
+          tma_load_4d(sbase + C::OFF_Q + a * C::BM * C::SWB, &tm_q, bar(B_QFULL), a * C::AE,
+                      tl.q0, tl.h, tl.b);
+        ++nq;
+        for (int j = 0; j < tl.nkv; ++j) {
+          const int g = gs + j, sk = g % C::NSTK;
+          if (g >= C::NSTK &&
+              !mbar_wait(bar(B_KEMPTY + sk), (uint32_t)(g / C::NSTK - 1) & 1u, wc)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar(B_KFULL + sk), C::KV_BYTES);
+          for (int a = 0; a < C::NAT; ++a)
+            tma_load_4d(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB, &tm_k,
+                        bar(B_KFULL + sk), a * C::AE, j * C::BN, tl.hk, tl.b);
+          loaded = g + 1;
+        }
+        gs += tl.nkv;
       }
       // After an abort, let the loads this thread issued land before the CTA exits.
       if (*abort_flag) {
-        mbar_wait_drain(bar(B_QFULL), 0, timeout_ns);
-        for (int j = max(0, loaded - C::NSTK); j < loaded; ++j)
-          mbar_wait_drain(bar(B_KFULL + j % C::NSTK), (uint32_t)(j / C::NSTK) & 1u, timeout_ns);
+        if (nq > 0) mbar_wait_drain(bar(B_QFULL), (uint32_t)(nq - 1) & 1u, timeout_ns);
+        for (int g = max(0, loaded - C::NSTK); g < loaded; ++g)
+          mbar_wait_drain(bar(B_KFULL + g % C::NSTK), (uint32_t)(g / C::NSTK) & 1u, timeout_ns);
       }
     } else if (lane == 1) {
       tma_prefetch_desc(&tm_v);
-      int loaded = 0;
-      for (int j = 0; j < nkv; ++j) {
-        const int sv = j % C::NSTV;
-        if (j >= C::NSTV &&
-            !mbar_wait(bar(B_VEMPTY + sv), (uint32_t)(j / C::NSTV - 1) & 1u, wc))
-          break;
-        loaded = j + 1;
-        // test hook (fa_sm100_set_debug_flags bit 0): never load the first V tile,
-        // so the PV issuer's wait for it runs out
-        if ((debug_flags & 1) && j == 0) continue;
-        mbar_arrive_expect_tx(bar(B_VFULL + sv), C::KV_BYTES);
-        for (int a = 0; a < C::NAT; ++a)
-          tma_load_4d(sbase + C::OFF_V + sv * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
-                      bar(B_VFULL + sv), a * C::AE, j * C::BN, hk, b);
+      int loaded = 0, gs = 0;
+      bool ok = true;
+      for (int t = 0; ok && t < rounds; ++t) {
+        Tile tl;
+        if (!tile_at(t, tl) || tl.nkv == 0) continue;
+        for (int j = 0; j < tl.nkv; ++j) {
+          const int g = gs + j, sv = g % C::NSTV;
+          if (g >= C::NSTV &&
+              !mbar_wait(bar(B_VEMPTY + sv), (uint32_t)(g / C::NSTV - 1) & 1u, wc)) {
+            ok = false;
+            break;
+          }
+          loaded = g + 1;
+          // test hook (fa_sm100_set_debug_flags bit 0): never load the CTA's first
+          // V tile, so the PV issuer's wait for it runs out
+          if ((debug_flags & 1) && g == 0) continue;
+          mbar_arrive_expect_tx(bar(B_VFULL + sv), C::KV_BYTES);
+          for (int a = 0; a < C::NAT; ++a)
+            tma_load_4d(sbase + C::OFF_V + sv * C::KV_BYTES + a * C::BN * C::SWB, &tm_v,
+                        bar(B_VFULL + sv), a * C::AE, j * C::BN, tl.hk, tl.b);
+        }
+        gs += tl.nkv;
       }
       if (*abort_flag) {
-        for (int j = max(0, loaded - C::NSTV); j < loaded; ++j) {
-          if ((debug_flags & 1) && j == 0) continue;
-          mbar_wait_drain(bar(B_VFULL + j % C::NSTV), (uint32_t)(j / C::NSTV) & 1u, timeout_ns);
+        for (int g = max(0, loaded - C::NSTV); g < loaded; ++g) {
+          if ((debug_flags & 1) && g == 0) continue;
+          mbar_wait_drain(bar(B_VFULL + g % C::NSTV), (uint32_t)(g / C::NSTV) & 1u, timeout_ns);
         }
       }
     }
@@ -243,14 +294,21 @@ __global__ void __launch_bounds__(608, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(C::BM, C::BN, false, false) | Elem<T>::kIdescAB;
       constexpr uint32_t swz = swizzle_field(C::SWB);
-      bool ok = mbar_wait(bar(B_QFULL), 0, wc);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int sk = j % C::NSTK, sb = j & 1;
-        if (!mbar_wait(bar(B_KFULL + sk), (uint32_t)(j / C::NSTK) & 1u, wc) ||
-            (j >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)))
+      bool ok = true;
+      int gs = 0, nq = 0;
+      for (int t = 0; ok && t < rounds; ++t) {
+       Tile tl;
+       if (!tile_at(t, tl) || tl.nkv == 0) continue;
+       if (!mbar_wait(bar(B_QFULL), (uint32_t)nq & 1u, wc)) break;
+       for (int j = 0; j < tl.nkv; ++j) {
+        const int g = gs + j, sk = g % C::NSTK, sb = g & 1;
+        if (!mbar_wait(bar(B_KFULL + sk), (uint32_t)(g / C::NSTK) & 1u, wc) ||
+            (g >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((g - 2) >> 1) & 1u, wc))) {
+          ok = false;
           break;
-        FTRACE(0, j);
-        if (j == 0) CTRACE(2);
+        }
+        FTRACE(0, g);
+        if (g == 0) CTRACE(2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -265,7 +323,12 @@ __global__ void __launch_bounds__(608, 1)
         }
         mma_commit(bar(B_SFULL + sb));
         mma_commit(bar(B_KEMPTY + sk));
-        FTRACE(1, j);
+        FTRACE(1, g);
+       }
+       if (!ok) break;
+       mma_commit(bar(B_QEMPTY));  // Q may be reloaded for the next tile
+       ++nq;
+       gs += tl.nkv;
       }
       mma_commit(bar(B_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
@@ -275,12 +338,20 @@ __global__ void __launch_bounds__(608, 1)
       constexpr uint32_t idesc_pv = make_idesc_f16(C::BM, D, false, true) | Elem<T>::kIdescAB;
       constexpr uint32_t swz = swizzle_field(C::SWB);
       bool ok = true;
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int sv = j % C::NSTV, pb = j & 1;
-        if (!mbar_wait(bar(B_PFULL + pb), (uint32_t)(j >> 1) & 1u, wc) ||
-            !mbar_wait(bar(B_VFULL + sv), (uint32_t)(j / C::NSTV) & 1u, wc))
+      int gs = 0, nt = 0;
+      for (int t = 0; ok && t < rounds; ++t) {
+       Tile tl;
+       if (!tile_at(t, tl) || tl.nkv == 0) continue;
+       // the first O += P V of a tile overwrites O: the previous epilogue must have read it
+       if (nt > 0 && !mbar_wait(bar(B_OFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
+       for (int j = 0; j < tl.nkv; ++j) {
+        const int g = gs + j, sv = g % C::NSTV, pb = g & 1;
+        if (!mbar_wait(bar(B_PFULL + pb), (uint32_t)(g >> 1) & 1u, wc) ||
+            !mbar_wait(bar(B_VFULL + sv), (uint32_t)(g / C::NSTV) & 1u, wc)) {
+          ok = false;
           break;
-        FTRACE(2, j);
+        }
+        FTRACE(2, g);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk) {
@@ -292,7 +363,10 @@ __global__ void __launch_bounds__(608, 1)
         mma_commit(bar(B_ODONE));
         mma_commit(bar(B_VEMPTY + sv));
         mma_commit(bar(B_PFREE + pb));
-        FTRACE(3, j);
+        FTRACE(3, g);
+       }
+       ++nt;
+       gs += tl.nkv;
       }
       mma_commit(bar(B_DRAIN));
     }
@@ -301,7 +375,6 @@ __global__ void __launch_bounds__(608, 1)
     const int lq = warp & 3;  // TMEM lane quarter (query rows 32*lq..)
     const int cq = warp >> 2;  // key-column quarter (32 columns of each key tile)
     const int r = lq * 32 + lane;
-    const int q_idx = q0 + r;
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
     constexpr int QC = C::BN / 4;                   // key columns per warp
     constexpr int EC = (D / 4 >= 16) ? D / 4 : 16;  // O columns per warp
@@ -309,146 +382,165 @@ __global__ void __launch_bounds__(608, 1)
     float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);  // [parity][cq][row]
     const uint32_t xbar = bar(B_XCHG + lq);
     const float NEG_INF = -__int_as_float(0x7f800000);
-    float m_run = NEG_INF;  // running max, already multiplied by scale*log2(e)
-    float l_run = 0.f;      // this warp's share of the row sum
     bool ok = true;
-    // stage(j): S of step j into registers (its buffer released at once), masked,
-    // and this quarter's row max posted to the exchange.  The loop stages step
-    // j + 1 right after step j's P values are computed, so the load and the four
-    // warps' exchange overlap step j's P store instead of stalling all of them
-    // together at the top of the next step.
-    auto stage = [&](int j, float (&dst)[QC]) -> bool {
-      const int sb = j & 1;
-      if (!mbar_wait(bar(B_SFULL + sb), (uint32_t)(j >> 1) & 1u, wc)) return false;
-      if (threadIdx.x == 0) FTRACE(8, j);
-      tc_fence_after();
-      tmem_ld32(tmem + lane_base + C::COL_S + sb * 128 + cq * QC,
-                *reinterpret_cast<uint32_t(*)[32]>(&dst[0]));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_SFREE + sb));
-      const int kv0 = j * C::BN + cq * QC;
-      const bool need_mask = (kv0 + QC > Sk) || (causal && kv0 + QC - 1 > q0 + off);
-      if (need_mask) {
-        const int lim = min(Sk - kv0, causal ? (q_idx + off - kv0 + 1) : QC);
-#pragma unroll
-        for (int c = 0; c < QC; ++c)
-          if (c >= lim) dst[c] = NEG_INF;
-      }
-      float mx[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) mx[u] = fmaxf(dst[u], dst[4 + u]);
-#pragma unroll
-      for (int c = 8; c < QC; c += 8)
-#pragma unroll
-        for (int u = 0; u < 4; ++u) mx[u] = fmax3(mx[u], dst[c + u], dst[c + 4 + u]);
-      float* xs = xch + (j & 1) * 512;
-      xs[cq * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xbar);
-      return true;
-    };
-    float sv[QC];
-    if (nkv > 0 && !stage(0, sv)) ok = false;
-    for (int j = 0; ok && j < nkv; ++j) {
-      const int sb = j & 1;
-      // row max over the four column quarters (posted one iteration earlier)
-      if (!mbar_wait(xbar, (uint32_t)j & 1u, wc)) { ok = false; break; }
-      const float* xs = xch + (j & 1) * 512;
-      const float mt = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
-      const float m_new = fmaxf(m_run, mt * scale_log2);
-      // Lazy rescale: keep the old reference max unless the row max grew by > 8
-      // (a factor 256 in P), or this is the first finite max of the row.
-      float m_use = m_run;
-      if (m_new > m_run + 8.0f || (m_run == NEG_INF && m_new != NEG_INF)) m_use = m_new;
-      const bool rescale = (m_use != m_run);
-      const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
-      const float m_safe = (m_use == NEG_INF) ? 0.f : m_use;
-      // p = 2^(s*scale*log2e - m) on packed pairs; one pair in four takes the
-      // FMA-pipe exp2 so the MUFU unit and the FMA pipe share the load.
-      const uint64_t c2 = f2_pack(scale_log2, scale_log2);
-      const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
-      uint64_t sum2 = f2_pack(0.f, 0.f);
-      uint32_t pp[QC / 2];
-#pragma unroll
-      for (int k = 0; k < QC / 2; ++k) {
-        const uint64_t x2 = f2_fma(f2_pack(sv[2 * k], sv[2 * k + 1]), c2, nm2);
-        uint64_t p2;
-        if ((k & 3) == 3) {
-          p2 = f2_exp2_poly(x2);
-        } else {
-          float x0, x1;
-          f2_unpack(x2, x0, x1);
-          p2 = f2_pack(ex2(x0), ex2(x1));
+    int gs = 0;  // steps of the earlier tiles
+    int xp = 0;  // exchange phases of the earlier tiles (one per step + the row sum)
+    for (int t = 0; ok && t < rounds; ++t) {
+      Tile tl;
+      if (!tile_at(t, tl)) continue;
+      const int q0 = tl.q0, nkv = tl.nkv;
+      const int q_idx = q0 + r;
+      if (nkv == 0) {
+        // every key is masked for these rows (only when Sq > Sk): O = 0, LSE = +inf
+        if (q_idx < Sq) {
+          T* orow = out + (((size_t)tl.b * Sq + q_idx) * H + tl.h) * D + cq * EC;
+          if (o_cols)
+            for (int c = 0; c < EC; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+          if (lse != nullptr && cq == 0) lse[(size_t)tl.bh * Sq + q_idx] = __int_as_float(0x7f800000);
         }
-        sum2 = f2_add(sum2, p2);
-        float p0, p1;
-        f2_unpack(p2, p0, p1);
-        pp[k] = Elem<T>::pack2(p0, p1);
+        continue;
       }
-      float lsum0, lsum1;
-      f2_unpack(sum2, lsum0, lsum1);
-      l_run = l_run * alpha + (lsum0 + lsum1);
-      if (threadIdx.x == 0) FTRACE(9, j);
-      // this step's scores are dead: stage the next step into their registers
-      if (j + 1 < nkv && !stage(j + 1, sv)) { ok = false; break; }
-      // P_b is free once O += P_b V of tile j-2 has read it
-      if (j >= 2 && !mbar_wait(bar(B_PFREE + sb), (uint32_t)((j - 2) >> 1) & 1u, wc)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      tmem_st16(tmem + lane_base + C::COL_P + sb * 64 + cq * (QC / 2), pp);
-      // Rescaling O needs O += P V of tile j-1 to have completed (rare: lazy rescale)
-      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        if (!mbar_wait(bar(B_ODONE), (uint32_t)(j - 1) & 1u, wc)) { ok = false; break; }
+      float m_run = NEG_INF;  // running max, already multiplied by scale*log2(e)
+      float l_run = 0.f;      // this warp's share of the row sum
+      // stage(j): S of step j into registers (its buffer released at once), masked,
+      // and this quarter's row max posted to the exchange.  The loop stages step
+      // j + 1 right after step j's P values are computed, so the load and the four
+      // warps' exchange overlap step j's P store instead of stalling all of them
+      // together at the top of the next step.
+      auto stage = [&](int j, float (&dst)[QC]) -> bool {
+        const int g = gs + j, sb = g & 1;
+        if (!mbar_wait(bar(B_SFULL + sb), (uint32_t)(g >> 1) & 1u, wc)) return false;
+        if (threadIdx.x == 0) FTRACE(8, g);
         tc_fence_after();
-        if (o_cols) {
+        tmem_ld32(tmem + lane_base + C::COL_S + sb * 128 + cq * QC,
+                  *reinterpret_cast<uint32_t(*)[32]>(&dst[0]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_SFREE + sb));
+        const int kv0 = j * C::BN + cq * QC;
+        const bool need_mask = (kv0 + QC > Sk) || (causal && kv0 + QC - 1 > q0 + off);
+        if (need_mask) {
+          const int lim = min(Sk - kv0, causal ? (q_idx + off - kv0 + 1) : QC);
 #pragma unroll
-          for (int c = 0; c < EC / 16; ++c) {
-            uint32_t o[16];
-            const uint32_t ta = tmem + lane_base + C::COL_O + cq * EC + c * 16;
-            tmem_ld16(ta, o);
-            tmem_wait_ld();
+          for (int c = 0; c < QC; ++c)
+            if (c >= lim) dst[c] = NEG_INF;
+        }
+        float mx[4];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(ta, o);
+        for (int u = 0; u < 4; ++u) mx[u] = fmaxf(dst[u], dst[4 + u]);
+#pragma unroll
+        for (int c = 8; c < QC; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mx[u] = fmax3(mx[u], dst[c + u], dst[c + 4 + u]);
+        float* xs = xch + ((xp + j) & 1) * 512;
+        xs[cq * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+        return true;
+      };
+      float sv[QC];
+      if (!stage(0, sv)) { ok = false; break; }
+      for (int j = 0; j < nkv; ++j) {
+        const int g = gs + j, sb = g & 1;
+        // row max over the four column quarters (posted one iteration earlier)
+        if (!mbar_wait(xbar, (uint32_t)(xp + j) & 1u, wc)) { ok = false; break; }
+        const float* xs = xch + ((xp + j) & 1) * 512;
+        const float mt = fmaxf(fmaxf(xs[r], xs[128 + r]), fmaxf(xs[256 + r], xs[384 + r]));
+        const float m_new = fmaxf(m_run, mt * scale_log2);
+        // Lazy rescale: keep the old reference max unless the row max grew by > 8
+        // (a factor 256 in P), or this is the first finite max of the row.
+        float m_use = m_run;
+        if (m_new > m_run + 8.0f || (m_run == NEG_INF && m_new != NEG_INF)) m_use = m_new;
+        const bool rescale = (m_use != m_run);
+        const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
+        const float m_safe = (m_use == NEG_INF) ? 0.f : m_use;
+        // p = 2^(s*scale*log2e - m) on packed pairs; one pair in four takes the
+        // FMA-pipe exp2 so the MUFU unit and the FMA pipe share the load.
+        const uint64_t c2 = f2_pack(scale_log2, scale_log2);
+        const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+        uint32_t pp[QC / 2];
+#pragma unroll
+        for (int k = 0; k < QC / 2; ++k) {
+          const uint64_t x2 = f2_fma(f2_pack(sv[2 * k], sv[2 * k + 1]), c2, nm2);
+          uint64_t p2;
+          if ((k & 3) == 3) {
+            p2 = f2_exp2_poly(x2);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            p2 = f2_pack(ex2(x0), ex2(x1));
+          }
+          sum2 = f2_add(sum2, p2);
+          float p0, p1;
+          f2_unpack(p2, p0, p1);
+          pp[k] = Elem<T>::pack2(p0, p1);
+        }
+        float lsum0, lsum1;
+        f2_unpack(sum2, lsum0, lsum1);
+        l_run = l_run * alpha + (lsum0 + lsum1);
+        if (threadIdx.x == 0) FTRACE(9, g);
+        // this step's scores are dead: stage the next step into their registers
+        if (j + 1 < nkv && !stage(j + 1, sv)) { ok = false; break; }
+        // P_b is free once O += P_b V of step g-2 has read it
+        if (g >= 2 && !mbar_wait(bar(B_PFREE + sb), (uint32_t)((g - 2) >> 1) & 1u, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + C::COL_P + sb * 64 + cq * (QC / 2), pp);
+        // Rescaling O needs O += P V of step g-1 to have completed (rare: lazy
+        // rescale; the first step of a tile overwrites O instead)
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          if (!mbar_wait(bar(B_ODONE), (uint32_t)(g - 1) & 1u, wc)) { ok = false; break; }
+          tc_fence_after();
+          if (o_cols) {
+#pragma unroll
+            for (int c = 0; c < EC / 16; ++c) {
+              uint32_t o[16];
+              const uint32_t ta = tmem + lane_base + C::COL_O + cq * EC + c * 16;
+              tmem_ld16(ta, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st16(ta, o);
+            }
           }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PFULL + sb));
+        if (threadIdx.x == 0) FTRACE(10, g);
+        m_run = m_use;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PFULL + sb));
-      if (threadIdx.x == 0) FTRACE(10, j);
-      m_run = m_use;
-    }
-    // ------------------------------------------------------------ epilogue
-    if (ok && nkv > 0) {
+      if (!ok) break;
+      // ---------------------------------------------------------- epilogue
       // A row that saw no finite score (every key masked: only when Sq > Sk)
       // keeps l = 0, i.e. O = 0 and LSE = +inf; the FMA-pipe exp2 returns 2^-125,
       // not 0, for masked scores, which only rows with a finite score may absorb.
       if (m_run == NEG_INF) l_run = 0.f;
       // the full row sum: the four column quarters' shares
-      float* xs = xch + (nkv & 1) * 512;
-      xs[cq * 128 + r] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xbar);
-      ok = mbar_wait(xbar, (uint32_t)nkv & 1u, wc);
-      if (ok) l_run = (xs[r] + xs[128 + r]) + (xs[256 + r] + xs[384 + r]);
-    }
-    // Wait for the last O += P V.  Its P-buffer barrier is unambiguous here (this
-    // thread observed that buffer's previous phase), unlike the every-PV ODONE
-    // barrier, which may still be two phases behind; a commit covers all of the
-    // issuing thread's earlier MMAs.
-    if (ok && nkv > 0 &&
-        mbar_wait(bar(B_PFREE + ((nkv - 1) & 1)), (uint32_t)((nkv - 1) >> 1) & 1u, wc)) {
+      {
+        float* xs = xch + ((xp + nkv) & 1) * 512;
+        xs[cq * 128 + r] = l_run;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+        if (!mbar_wait(xbar, (uint32_t)(xp + nkv) & 1u, wc)) { ok = false; break; }
+        l_run = (xs[r] + xs[128 + r]) + (xs[256 + r] + xs[384 + r]);
+      }
+      // Wait for the tile's last O += P V.  Its P-buffer barrier is unambiguous
+      // here (this thread observed that buffer's previous phase), unlike the
+      // every-PV ODONE barrier, which may still be two phases behind; a commit
+      // covers all of the issuing thread's earlier MMAs.
+      const int gl = gs + nkv - 1;
+      if (!mbar_wait(bar(B_PFREE + (gl & 1)), (uint32_t)(gl >> 1) & 1u, wc)) { ok = false; break; }
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-      const bool row_ok = q_idx < Sq;
-      T* orow = out + (((size_t)b * Sq + q_idx) * H + h) * D + cq * EC;
       if (o_cols) {
+        const bool row_ok = q_idx < Sq;
+        T* orow = out + (((size_t)tl.b * Sq + q_idx) * H + tl.h) * D + cq * EC;
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
           uint32_t o[16];
@@ -469,18 +561,17 @@ __global__ void __launch_bounds__(608, 1)
           }
         }
       }
-      if (lse != nullptr && row_ok && cq == 0) {
+      // O has been read: the next tile's first O += P V may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_OFREE));
+      if (lse != nullptr && q_idx < Sq && cq == 0) {
         const float m_safe = (m_run == NEG_INF) ? 0.f : m_run;
-        lse[(size_t)bh * Sq + q_idx] =
+        lse[(size_t)tl.bh * Sq + q_idx] =
             l_run > 0.f ? (m_safe + lg2(l_run)) * 0.69314718055994530942f : __int_as_float(0x7f800000);
       }
-    }
-    if (nkv == 0 && q_idx < Sq) {
-      // every key is masked for these rows (only when Sq > Sk): O = 0, LSE = +inf
-      T* orow = out + (((size_t)b * Sq + q_idx) * H + h) * D + cq * EC;
-      if (o_cols)
-        for (int c = 0; c < EC; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-      if (lse != nullptr && cq == 0) lse[(size_t)bh * Sq + q_idx] = __int_as_float(0x7f800000);
+      gs += nkv;
+      xp += nkv + 1;
     }
   }
 
@@ -502,10 +593,14 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   constexpr int tag = D + (std::is_same<T, __half>::value ? 0 : 1000);
   if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_fwd_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.H * ((a.Sq + C::BM - 1) / C::BM));
+  const int ntiles = a.B * a.H * ((a.Sq + C::BM - 1) / C::BM);
+  const int nsm = sm_count();
+  if (nsm <= 0) return FA_ERR_DEVICE;
+  dim3 grid(ntiles < nsm ? ntiles : nsm);  // persistent: one CTA per SM
   const cudaError_t e = launch_pdl(fa_fwd_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream,
                                    *a.tm_q, *a.tm_k, *a.tm_v, static_cast<T*>(a.o), a.lse,
-                                   a.Sq, a.Sk, a.H, a.H / a.Hkv, a.scale * 1.4426950408889634f,
+                                   a.Sq, a.Sk, a.H, a.H / a.Hkv, ntiles,
+                                   a.scale * 1.4426950408889634f,
                                    a.causal,
                                    a.status, a.timeout_ns, a.debug_flags);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;

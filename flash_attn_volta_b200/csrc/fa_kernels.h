@@ -75,6 +75,20 @@ bool smem_attr_set(const void* func, int bytes) {
   done.fetch_or(bit, std::memory_order_acq_rel);
   return true;
 }
+// Streaming multiprocessors of the current device (cached per device; 0 on error).
+inline int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
 }  // namespace
 
 // Launch with programmatic stream serialization: the kernel may start while the

@@ -20,8 +20,11 @@
 // Kernels:
 //   fa_bwd_pre   delta = rowsum(O * dO), the extra K-step rows of Q and dO in the
 //                MMA's no-swizzle K-major layout, zero the dQ accumulator.
-//   fa_bwd_main  one CTA = one 128-row key/value tile of one (batch, head);
-//                loops over query tiles of BM rows (64 for D=128, else 128).
+//   fa_bwd_main  persistent, one CTA per SM over a list of 128-row key/value
+//                tiles of the (batch, K/V head) pairs; each tile loops over
+//                query tiles of BM rows (64 for D=128, else 128).  The next
+//                tile's K/V load, Q/dO loads and first S^T / dP^T MMAs overlap
+//                this tile's last iterations and its dK/dV epilogue.
 //     warps 0-7  "softmax": warp w owns key rows 32*(w%4).. (its TMEM lane
 //                quarter) and half of the query columns.  Loads S^T and dP^T
 //                from tensor memory into registers and releases them at once
@@ -33,8 +36,10 @@
 //     warps 8-11 dQ epilogue: read this tile's dQ partial from tensor memory,
 //                stage it in shared memory and add it into the fp32 accumulator
 //                with one bulk reduction (cp.reduce.async.bulk .add.f32).
-//     warp 12    TMA producer (K, V once; Q, dO and their extra K-step rows per
-//                query tile).
+//     warp 12    TMA producers: lane 0 K and V of each key tile (once the last
+//                MMAs reading the previous tile's have completed); lane 1 Q,
+//                dO and their extra K-step rows per query tile (a 3-stage ring
+//                that runs across key tiles).
 //     warps 13-16 MMA issuers, one per independent chain: S^T = K Q^T,
 //                dP^T = V dO^T (issued as soon as the previous tile's values are
 //                in registers), dV += P^T dO with dK += dS^T Q, and the dQ
@@ -132,7 +137,9 @@ enum BwdBar {
   C_DQFREE = 13,  // 4 arrivals
   C_KVDONE = 14,
   C_DRAIN = 15,   // 4 arrivals: each MMA issuer's last commit
-  C_COUNT = 16
+  C_KVEMPTY = 16,  // 3 arrivals: a tile's last S^T, dP^T and dQ MMAs have read K / V
+  C_DKVFREE = 17,  // 8 arrivals: the epilogue has read dK / dV
+  C_COUNT = 18
 };
 
 // -------------------------------------------------------------------------- pre
@@ -238,6 +245,9 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restri
 }
 
 // -------------------------------------------------------------------------- main
+// K/V heads per window of the backward's tile list.
+constexpr int kBwdHeadWindow = 16;
+
 template <int D, typename T>
 __global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -247,7 +257,7 @@ __global__ void __launch_bounds__(544, 1)
                        const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
                        float* __restrict__ dq_acc,
                        T* __restrict__ dk, T* __restrict__ dv, int Sq, int Sk, int H, int group,
-                       int S_pad,
+                       int S_pad, int ntiles,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
   using C = BwdCfg<D>;
@@ -270,28 +280,45 @@ __global__ void __launch_bounds__(544, 1)
     if (blockIdx.x < 8192) g_bcta[blockIdx.x][0] = smid;
 #endif
   }
-  // 1-D grid over (head group, key block, K/V head): key block 0 (the most
-  // query tiles under a causal mask) first inside each group of heads.  With
-  // grouped-query attention (`group` query heads per K/V head) the CTA runs
-  // through every query head of its group, so dK / dV sum over the group in
-  // tensor memory.
+  // Persistent: the CTA walks a list of 128-row key tiles.  Tile list: (window
+  // of kBwdHeadWindow K/V heads, key block, K/V head), key block 0 (the most
+  // query tiles under a causal mask) first inside each window; round t gives
+  // this CTA tile t * grid + pos, pos = blockIdx.x on even rounds and its
+  // mirror on odd ones.  With grouped-query attention (`group` query heads per
+  // K/V head) a tile runs through every query head of its group, so dK / dV
+  // sum over the group in tensor memory.  Barrier phases count iterations (and
+  // tiles) over the whole list.
   const int nkt = (Sk + C::BN - 1) / C::BN;
   const int Hkv = H / group;
-  int bhk, kt;
-  grid_to_tile((int)blockIdx.x, (int)(gridDim.x / nkt), nkt, kHeadGroup, bhk, kt);
-  const int b = bhk / Hkv, hk = bhk % Hkv;
-  const int kv0 = kt * C::BN;
+  const int rounds = (ntiles + (int)gridDim.x - 1) / (int)gridDim.x;
   const int ntq = (Sq + C::BM - 1) / C::BM;
   // causal mask aligned to the bottom-right: query i sees keys j <= i + Sk - Sq
   const int off = Sk - Sq;
-  // first query tile that sees this key tile
-  const int i0 = causal ? max(0, kv0 - off) / C::BM : 0;
-  const int nq = max(0, ntq - i0);          // query tiles per query head
-  const int nit = group * nq;               // iterations: (query head, query tile)
-  // iteration it: query head hk * group + it / nq, first row of query tile i0 + it % nq
-  // (no division for plain multi-head attention: it sits on the softmax warps' path)
-  auto q_head = [&](int it) { return group == 1 ? hk : hk * group + it / nq; };
-  auto q_row0 = [&](int it) { return (i0 + (group == 1 ? it : it % nq)) * C::BM; };
+  struct KTile {
+    int b, hk, kv0, i0, nq, nit;
+  };
+  auto tile_at = [&](int t, KTile& tl) -> bool {
+    const int pos = (t & 1) ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int L = t * (int)gridDim.x + pos;
+    if (L >= ntiles) return false;
+    int bhk, kt;
+    grid_to_tile(L, ntiles / nkt, nkt, kBwdHeadWindow, bhk, kt);
+    tl.b = bhk / Hkv;
+    tl.hk = bhk % Hkv;
+    tl.kv0 = kt * C::BN;
+    // first query tile that sees this key tile
+    tl.i0 = causal ? max(0, tl.kv0 - off) / C::BM : 0;
+    tl.nq = max(0, ntq - tl.i0);  // query tiles per query head
+    tl.nit = group * tl.nq;       // iterations: (query head, query tile)
+    return true;
+  };
+  // iteration it of a tile: query head hk * group + it / nq, first row of query
+  // tile i0 + it % nq (no division for plain multi-head attention: it sits on
+  // the softmax warps' path)
+  auto q_head = [&](const KTile& tl, int it) { return group == 1 ? tl.hk : tl.hk * group + it / tl.nq; };
+  auto q_row0 = [&](const KTile& tl, int it) {
+    return (tl.i0 + (group == 1 ? it : it % tl.nq)) * C::BM;
+  };
 
   WaitCtx wc{abort_flag, status, timeout_ns};
 
@@ -301,6 +328,8 @@ __global__ void __launch_bounds__(544, 1)
       if (i == C_SFREE || i == C_DSREADY) cnt = 8;
       if (i == C_SFULL || i == C_PFREE) cnt = 2;  // two issuing threads commit
       if (i == C_DQFREE || i == C_DRAIN) cnt = 4;
+      if (i == C_KVEMPTY) cnt = 3;
+      if (i == C_DKVFREE) cnt = 8;
       mbar_init(bar(i), cnt);
     }
     *abort_flag = 0;
@@ -331,47 +360,81 @@ __global__ void __launch_bounds__(544, 1)
   }
 
   if (warp == 12) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producers
+    // Lane 0: K and V of each tile (the next tile's once the last MMAs reading
+    // this tile's have completed); lane 1: the Q / dO ring, which runs on into
+    // the next tile's query tiles meanwhile.
+    auto load_kv = [&](const KTile& tl) {
+      mbar_arrive_expect_tx(bar(C_KVFULL), 2 * C::KV_BYTES);
+      for (int a = 0; a < C::NAT; ++a) {
+        tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE,
+                    tl.kv0, tl.hk, tl.b);
+        tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE,
+                    tl.kv0, tl.hk, tl.b);
+      }
+    };
+    // K and V were written before the previous kernel: the first tile's load
+    // goes out before the wait for it.
+    int t_first = 0;
+    KTile first{};
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_do);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar(C_KVFULL), 2 * C::KV_BYTES);
-      for (int a = 0; a < C::NAT; ++a) {
-        tma_load_4d(sbase + C::OFF_K + a * C::BN * C::SWB, &tm_k, bar(C_KVFULL), a * C::AE, kv0, hk, b);
-        tma_load_4d(sbase + C::OFF_V + a * C::BN * C::SWB, &tm_v, bar(C_KVFULL), a * C::AE, kv0, hk, b);
-      }
+      for (; t_first < rounds; ++t_first)
+        if (tile_at(t_first, first) && first.nit > 0) break;
+      if (t_first < rounds) load_kv(first);
     }
     griddep_wait();
     griddep_launch_dependents();
     if (lane == 0) {
-      int q_last[C::NST];  // last query tile loaded into each stage
-      for (int t = 0; t < C::NST; ++t) q_last[t] = -1;
-      for (int it = 0; it < nit; ++it) {
-        const int st = it % C::NST;
-        const uint32_t ph = (uint32_t)(it / C::NST) & 1u;
-        const int q0 = q_row0(it), h = q_head(it);
-        TRACE(0, it);
-        if (it >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) break;
-        TRACE(1, it);
-        mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::AUG_BYTES);
-        for (int a = 0; a < C::NAT; ++a) {
-          tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
-                      bar(C_QFULL + st), a * C::AE, q0, h, b);
-          tma_load_4d(sbase + C::OFF_DO + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_do,
-                      bar(C_QFULL + st), a * C::AE, q0, h, b);
-        }
-        const size_t aug = ((size_t)(b * H + h) * S_pad + q0) * kAugRowBytes;
-        bulk_load(sbase + C::OFF_QA + st * C::AUG_BYTES, q_aug + aug, C::AUG_BYTES,
-                  bar(C_QFULL + st));
-        bulk_load(sbase + C::OFF_DA + st * C::AUG_BYTES, do_aug + aug, C::AUG_BYTES,
-                  bar(C_QFULL + st));
-        q_last[st] = it;
+      int nkv = t_first < rounds ? 1 : 0;  // K/V loads issued
+      for (int t = t_first + 1; t < rounds; ++t) {
+        KTile tl;
+        if (!tile_at(t, tl) || tl.nit == 0) continue;
+        if (!mbar_wait(bar(C_KVEMPTY), (uint32_t)(nkv - 1) & 1u, wc)) break;
+        load_kv(tl);
+        ++nkv;
       }
-      // After an abort, let the loads this CTA issued land before it exits.
+      // After an abort, let the loads this thread issued land before the CTA exits.
+      if (*abort_flag && nkv > 0) mbar_wait_drain(bar(C_KVFULL), (uint32_t)(nkv - 1) & 1u, timeout_ns);
+    } else if (lane == 1) {
+      int q_last[C::NST];  // last iteration loaded into each stage
+      for (int t = 0; t < C::NST; ++t) q_last[t] = -1;
+      int gs = 0;  // iterations of the earlier tiles
+      bool ok = true;
+      for (int t = 0; ok && t < rounds; ++t) {
+        KTile tl;
+        if (!tile_at(t, tl) || tl.nit == 0) continue;
+        for (int it = 0; it < tl.nit; ++it) {
+          const int gi = gs + it;
+          const int st = gi % C::NST;
+          const uint32_t ph = (uint32_t)(gi / C::NST) & 1u;
+          const int q0 = q_row0(tl, it), h = q_head(tl, it);
+          TRACE(0, gi);
+          if (gi >= C::NST && !mbar_wait(bar(C_QEMPTY + st), ph ^ 1u, wc)) {
+            ok = false;
+            break;
+          }
+          TRACE(1, gi);
+          mbar_arrive_expect_tx(bar(C_QFULL + st), 2 * C::Q_BYTES + 2 * C::AUG_BYTES);
+          for (int a = 0; a < C::NAT; ++a) {
+            tma_load_4d(sbase + C::OFF_Q + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_q,
+                        bar(C_QFULL + st), a * C::AE, q0, h, tl.b);
+            tma_load_4d(sbase + C::OFF_DO + st * C::Q_BYTES + a * C::BM * C::SWB, &tm_do,
+                        bar(C_QFULL + st), a * C::AE, q0, h, tl.b);
+          }
+          const size_t aug = ((size_t)(tl.b * H + h) * S_pad + q0) * kAugRowBytes;
+          bulk_load(sbase + C::OFF_QA + st * C::AUG_BYTES, q_aug + aug, C::AUG_BYTES,
+                    bar(C_QFULL + st));
+          bulk_load(sbase + C::OFF_DA + st * C::AUG_BYTES, do_aug + aug, C::AUG_BYTES,
+                    bar(C_QFULL + st));
+          q_last[st] = gi;
+        }
+        gs += tl.nit;
+      }
       if (*abort_flag) {
-        mbar_wait_drain(bar(C_KVFULL), 0, timeout_ns);
         for (int t = 0; t < C::NST; ++t)
           if (q_last[t] >= 0)
             mbar_wait_drain(bar(C_QFULL + t), (uint32_t)(q_last[t] / C::NST) & 1u, timeout_ns);
@@ -399,18 +462,27 @@ __global__ void __launch_bounds__(544, 1)
       constexpr uint32_t id_kv = make_idesc_f16(C::BN, D, false, true) | ab;      // dV, dK
       constexpr uint32_t id_dq = (C::DQT ? make_idesc_f16(D, C::BM, true, true)    // dQ^T
                                          : make_idesc_f16(C::BM, D, true, true)) | ab;  // dQ
-      bool ok = mbar_wait(bar(C_KVFULL), 0, wc);
-      for (int it = 0; ok && it < nit; ++it) {
-        const int st = it % C::NST;
+      bool ok = true;
+      int gs = 0, nt = 0;  // iterations and (non-empty) tiles before this one
+      for (int t = 0; ok && t < rounds; ++t) {
+       KTile tl;
+       if (!tile_at(t, tl) || tl.nit == 0) continue;
+       if (role != 2 && !mbar_wait(bar(C_KVFULL), (uint32_t)nt & 1u, wc)) break;
+       // the first dV / dK MMAs of a tile overwrite the accumulators: the
+       // previous tile's epilogue must have read them
+       if (role == 2 && nt > 0 && !mbar_wait(bar(C_DKVFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
+       for (int it = 0; it < tl.nit; ++it) {
+        const int gi = gs + it;
+        const int st = gi % C::NST;
         const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
         const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
         if (role <= 1) {
           // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
-          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(it / C::NST) & 1u, wc)) break;
-          if (role == 0) TRACE(15, it);
-          if (it > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(it - 1) & 1u, wc)) break;
-          if (role == 0) TRACE(2, it);
-          if (role == 0 && it == 0) CTRACE(2);
+          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc)) { ok = false; break; }
+          if (role == 0) TRACE(15, gi);
+          if (gi > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(gi - 1) & 1u, wc)) { ok = false; break; }
+          if (role == 0) TRACE(2, gi);
+          if (role == 0 && gi == 0) CTRACE(2);
           tc_fence_after();
           const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
           const uint32_t bbase = role == 0 ? qb : dob;
@@ -429,10 +501,10 @@ __global__ void __launch_bounds__(544, 1)
                                     128, 256, 0),
                      id_s, 1u);
           mma_commit(bar(C_SFULL));
-          if (role == 0) TRACE(3, it);
+          if (role == 0) TRACE(3, gi);
         } else if (role == 2) {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)it & 1u, wc)) break;
-          TRACE(4, it);
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc)) { ok = false; break; }
+          TRACE(4, gi);
           tc_fence_after();
           // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
 #pragma unroll
@@ -456,12 +528,14 @@ __global__ void __launch_bounds__(544, 1)
           }
           mma_commit(bar(C_QEMPTY + st));
           mma_commit(bar(C_PFREE));
-          TRACE(6, it);
+          TRACE(6, gi);
         } else {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)it & 1u, wc) ||
-              (it > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(it - 1) & 1u, wc)))
+          if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc) ||
+              (gi > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(gi - 1) & 1u, wc))) {
+            ok = false;
             break;
-          TRACE(5, it);
+          }
+          TRACE(5, gi);
           tc_fence_after();
           // dQ partial over this key tile (K = 128 key rows)
 #pragma unroll
@@ -478,8 +552,13 @@ __global__ void __launch_bounds__(544, 1)
           mma_commit(bar(C_DQFULL));
           mma_commit(bar(C_PFREE));
         }
+       }
+       if (!ok) break;
+       if (role == 2) mma_commit(bar(C_KVDONE));  // dK / dV of this tile complete
+       else mma_commit(bar(C_KVEMPTY));           // K / V may be reloaded
+       gs += tl.nit;
+       ++nt;
       }
-      if (role == 2) mma_commit(bar(C_KVDONE));
       mma_commit(bar(C_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
   } else if (warp < 8) {
@@ -487,20 +566,37 @@ __global__ void __launch_bounds__(544, 1)
     const int lq = warp & 3;         // TMEM lane quarter
     const int hf = warp >> 2;        // which half of the query columns
     const int r = lq * 32 + lane;    // key row inside the tile == TMEM lane
-    const int kv_idx = kv0 + r;
-    const bool kv_ok = kv_idx < Sk;
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
     const int c0 = hf * HW;          // first query column of this thread
+    constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // dK / dV epilogue columns per warp
     bool ok = true;
-    for (int it = 0; it < nit; ++it) {
-      const int st = it % C::NST;
-      const int q0 = q_row0(it);
-      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(it / C::NST) & 1u, wc) ||
-          !mbar_wait(bar(C_SFULL), (uint32_t)it & 1u, wc)) {
+    int gs = 0, nt = 0;  // iterations and (non-empty) tiles before this one
+    for (int t = 0; ok && t < rounds; ++t) {
+     KTile tl;
+     if (!tile_at(t, tl)) continue;
+     const int kv0 = tl.kv0, nit = tl.nit;
+     const int kv_idx = kv0 + r;
+     const bool kv_ok = kv_idx < Sk;
+     if (nit == 0) {
+       // no query row sees this key tile (Sq < Sk): dK = dV = 0
+       const size_t row_off = (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
+       if (kv_ok && hf * EC < D)
+         for (int c = 0; c < EC; c += 8) {
+           *reinterpret_cast<uint4*>(dv + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
+           *reinterpret_cast<uint4*>(dk + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
+         }
+       continue;
+     }
+     for (int it = 0; it < nit; ++it) {
+      const int gi = gs + it;
+      const int st = gi % C::NST;
+      const int q0 = q_row0(tl, it);
+      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc) ||
+          !mbar_wait(bar(C_SFULL), (uint32_t)gi & 1u, wc)) {
         ok = false;
         break;
       }
-      if (threadIdx.x == 0) TRACE(7, it);
+      if (threadIdx.x == 0) TRACE(7, gi);
       tc_fence_after();
       // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
       // dP^T are released after the last chunk's loads; P^T / dS^T are written only
@@ -514,12 +610,12 @@ __global__ void __launch_bounds__(544, 1)
         tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
         tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
         tmem_wait_ld();
-        if (threadIdx.x == 0 && cc == 0) TRACE(14, it);
+        if (threadIdx.x == 0 && cc == 0) TRACE(14, gi);
         if (cc == HW / 32 - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(C_SFREE));
-          if (threadIdx.x == 0) TRACE(8, it);
+          if (threadIdx.x == 0) TRACE(8, gi);
         }
         // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
         // dP'^T already hold -LSE/scale and -delta).  Only tiles that cross the
@@ -559,12 +655,12 @@ __global__ void __launch_bounds__(544, 1)
           }
         }
         if (cc == 0) {
-          if (threadIdx.x == 0) TRACE(11, it);
-          if (it > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(it - 1) & 1u, wc)) {
+          if (threadIdx.x == 0) TRACE(11, gi);
+          if (gi > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(gi - 1) & 1u, wc)) {
             ok = false;
             break;
           }
-          if (threadIdx.x == 0) TRACE(9, it);
+          if (threadIdx.x == 0) TRACE(9, gi);
         }
         // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
         // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
@@ -584,28 +680,23 @@ __global__ void __launch_bounds__(544, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C_DSREADY));
-      if (threadIdx.x == 0) TRACE(10, it);
-    }
-    // ------------------------------------------------------------ dK / dV epilogue
-    constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // columns per warp
-    if (ok && hf * EC < D && mbar_wait(bar(C_KVDONE), 0, wc)) {
-      tc_fence_after();
-      T* dvrow = dv + (((size_t)b * Sk + kv_idx) * Hkv + hk) * D;
-      T* dkrow = dk + (((size_t)b * Sk + kv_idx) * Hkv + hk) * D;
+      if (threadIdx.x == 0) TRACE(10, gi);
+     }
+     if (!ok) break;
+     // ---------------------------------------------------------- dK / dV epilogue
+     if (!mbar_wait(bar(C_KVDONE), (uint32_t)nt & 1u, wc)) { ok = false; break; }
+     tc_fence_after();
+     if (hf * EC < D) {
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
         const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
         const float f = pass == 0 ? 1.f : scale;
-        T* dst = (pass == 0 ? dvrow : dkrow) + hf * EC;
+        T* dst = (pass == 0 ? dv : dk) + (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
 #pragma unroll
         for (int c = 0; c < EC / 16; ++c) {
           uint32_t v[16];
           tmem_ld16(tmem + lane_base + col + c * 16, v);
           tmem_wait_ld();
-          if (nit == 0) {  // no query row sees this key tile (Sq < Sk): dK = dV = 0
-#pragma unroll
-            for (int u = 0; u < 16; ++u) v[u] = 0u;
-          }
           uint4 w0, w1;
           w0.x = Elem<T>::pack2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
           w0.y = Elem<T>::pack2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
@@ -621,6 +712,13 @@ __global__ void __launch_bounds__(544, 1)
           }
         }
       }
+     }
+     // dK / dV have been read: the next tile's first dV / dK MMAs may overwrite them
+     tc_fence_before();
+     __syncwarp();
+     if (lane == 0) mbar_arrive(bar(C_DKVFREE));
+     gs += nit;
+     ++nt;
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------ dQ epilogue warps 8..11
@@ -629,13 +727,19 @@ __global__ void __launch_bounds__(544, 1)
     const int wq = warp - 8;
     const int tid = threadIdx.x - 256;  // 0..127
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    for (int it = 0; it < nit; ++it) {
-      const int q0 = q_row0(it);
-      const int bh = b * H + q_head(it);
-      const int sbuf = it % C::NDQ;
+    bool ok = true;
+    int gs = 0;  // iterations of the earlier tiles
+    for (int t = 0; ok && t < rounds; ++t) {
+     KTile tl;
+     if (!tile_at(t, tl) || tl.nit == 0) continue;
+     for (int it = 0; it < tl.nit; ++it) {
+      const int gi = gs + it;
+      const int q0 = q_row0(tl, it);
+      const int bh = tl.b * H + q_head(tl, it);
+      const int sbuf = gi % C::NDQ;
       const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
-      if (!mbar_wait(bar(C_DQFULL), (uint32_t)it & 1u, wc)) break;
-      if (tid == 0) TRACE(12, it);
+      if (!mbar_wait(bar(C_DQFULL), (uint32_t)gi & 1u, wc)) { ok = false; break; }
+      if (tid == 0) TRACE(12, gi);
       tc_fence_after();
       if constexpr (C::DQT) {
         // TMEM lane = d, column = query row
@@ -694,8 +798,10 @@ __global__ void __launch_bounds__(544, 1)
       if (tid == 0) {
         bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
         bulk_commit_group();
-        TRACE(13, it);
+        TRACE(13, gi);
       }
+     }
+     gs += tl.nit;
     }
     if (tid == 0) bulk_wait_group_all();
   }
@@ -718,11 +824,15 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000);
   if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T>), C::SMEM))
     return FA_ERR_LAUNCH;
-  dim3 grid(a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN));
+  const int ntiles = a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN);
+  const int nsm = sm_count();
+  if (nsm <= 0) return FA_ERR_DEVICE;
+  dim3 grid(ntiles < nsm ? ntiles : nsm);  // persistent: one CTA per SM
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
       *a.tm_k, *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<T*>(a.dk), static_cast<T*>(a.dv),
-      a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, a.scale, a.scale * 1.4426950408889634f, a.causal,
+      a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, ntiles, a.scale, a.scale * 1.4426950408889634f,
+      a.causal,
       a.status,
       a.timeout_ns);
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;

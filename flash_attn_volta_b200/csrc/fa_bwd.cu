@@ -20,11 +20,13 @@
 // Kernels:
 //   fa_bwd_pre   delta = rowsum(O * dO), the extra K-step rows of Q and dO in the
 //                MMA's no-swizzle K-major layout, zero the dQ accumulator.
-//   fa_bwd_main  persistent, one CTA per SM over a list of 128-row key/value
-//                tiles of the (batch, K/V head) pairs; each tile loops over
-//                query tiles of BM rows (64 for D=128, else 128).  The next
-//                tile's K/V load, Q/dO loads and first S^T / dP^T MMAs overlap
-//                this tile's last iterations and its dK/dV epilogue.
+//   fa_bwd_main  a CTA walks a list of 128-row key/value tiles of the (batch,
+//                K/V head) pairs (persistent, one CTA per SM, for at most 4
+//                tiles per SM; else one CTA per tile); each tile loops over
+//                query tiles of BM rows (64 for D=128, else 128).  On the
+//                persistent grid the next tile's K/V load, Q/dO loads and first
+//                S^T / dP^T MMAs overlap this tile's last iterations and its
+//                dK/dV epilogue.
 //     warps 0-7  "softmax": warp w owns key rows 32*(w%4).. (its TMEM lane
 //                quarter) and half of the query columns.  Loads S^T and dP^T
 //                from tensor memory into registers and releases them at once
@@ -245,9 +247,6 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restri
 }
 
 // -------------------------------------------------------------------------- main
-// K/V heads per window of the backward's tile list.
-constexpr int kBwdHeadWindow = 16;
-
 template <int D, typename T>
 __global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -257,7 +256,7 @@ __global__ void __launch_bounds__(544, 1)
                        const uint8_t* __restrict__ q_aug, const uint8_t* __restrict__ do_aug,
                        float* __restrict__ dq_acc,
                        T* __restrict__ dk, T* __restrict__ dv, int Sq, int Sk, int H, int group,
-                       int S_pad, int ntiles,
+                       int S_pad, int ntiles, int win,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
   using C = BwdCfg<D>;
@@ -280,8 +279,8 @@ __global__ void __launch_bounds__(544, 1)
     if (blockIdx.x < 8192) g_bcta[blockIdx.x][0] = smid;
 #endif
   }
-  // Persistent: the CTA walks a list of 128-row key tiles.  Tile list: (window
-  // of kBwdHeadWindow K/V heads, key block, K/V head), key block 0 (the most
+  // The CTA walks a list of 128-row key tiles (one tile when the grid has a
+  // CTA per tile).  Tile list: (window of `win` K/V heads, key block, K/V head), key block 0 (the most
   // query tiles under a causal mask) first inside each window; round t gives
   // this CTA tile t * grid + pos, pos = blockIdx.x on even rounds and its
   // mirror on odd ones.  With grouped-query attention (`group` query heads per
@@ -302,7 +301,7 @@ __global__ void __launch_bounds__(544, 1)
     const int L = t * (int)gridDim.x + pos;
     if (L >= ntiles) return false;
     int bhk, kt;
-    grid_to_tile(L, ntiles / nkt, nkt, kBwdHeadWindow, bhk, kt);
+    grid_to_tile(L, ntiles / nkt, nkt, win, bhk, kt);
     tl.b = bhk / Hkv;
     tl.hk = bhk % Hkv;
     tl.kv0 = kt * C::BN;
@@ -827,11 +826,13 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   const int ntiles = a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN);
   const int nsm = sm_count();
   if (nsm <= 0) return FA_ERR_DEVICE;
-  dim3 grid(ntiles < nsm ? ntiles : nsm);  // persistent: one CTA per SM
+  const int g = tile_grid(ntiles, nsm);
+  dim3 grid(g);
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
       *a.tm_k, *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<T*>(a.dk), static_cast<T*>(a.dv),
-      a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, ntiles, a.scale, a.scale * 1.4426950408889634f,
+      a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, ntiles, tile_window(ntiles, g), a.scale,
+      a.scale * 1.4426950408889634f,
       a.causal,
       a.status,
       a.timeout_ns);

@@ -7,11 +7,12 @@
 // (B, S, H, D) fp16 tensors (row stride H*D), every head_dim in {16,32,64,128}
 // runs natively (no zero padding), and O is written in (B, S, H, D).
 //
-// Persistent: one CTA per SM walks a list of 128-row query tiles of the
-// (batch, head) pairs (round r takes tile r * grid + CTA, in reverse CTA order
-// on odd rounds, over a longest-first order), so the set-up is paid once per SM
-// and the next tile's Q load and first S = Q K^T overlap this tile's last
-// softmax step and its epilogue.  Tensor memory (512
+// A CTA walks a list of 128-row query tiles of the (batch, head) pairs (round
+// r takes tile r * grid + CTA, in reverse CTA order on odd rounds, over a
+// longest-first order).  Small problems (at most 4 tiles per SM) run one
+// persistent CTA per SM, so the set-up is paid once per SM and the next tile's
+// Q load and first S = Q K^T overlap this tile's last softmax step and its
+// epilogue; larger ones run one CTA per tile.  Tensor memory (512
 // columns): S0 [0,128), S1 [128,256) — S = Q K_j^T double-buffered; P0
 // [256,320), P1 [320,384) — P (fp16 pairs) double-buffered; O [384, 384+D).
 // Because P has its own columns, nothing in the tensor-core stream waits for
@@ -126,15 +127,11 @@ enum FwdBar {
   B_COUNT = 33
 };
 
-// Heads per window of the forward's tile list (K/V of 16 heads at S = 8192,
-// D = 128: 64 MiB, within L2).
-constexpr int kFwdHeadWindow = 16;
-
 template <int D, typename T>
 __global__ void __launch_bounds__(608, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
-                  float* __restrict__ lse, int Sq, int Sk, int H, int group, int ntiles,
+                  float* __restrict__ lse, int Sq, int Sk, int H, int group, int ntiles, int win,
                   float scale_log2, int causal,
                   int* status, unsigned long long timeout_ns, int debug_flags) {
   using C = FwdCfg<D>;
@@ -156,7 +153,7 @@ __global__ void __launch_bounds__(608, 1)
     if (blockIdx.x < 8192) g_fcta[blockIdx.x][0] = smid;
 #endif
   }
-  // Tile list: ntiles tiles in the order (window of kFwdHeadWindow heads, query
+  // Tile list: ntiles tiles in the order (window of `win` heads, query
   // block rank, head), longest blocks first inside each window so that K/V of
   // only a few heads live at once (L2 reuse) while the tiles dealt out in one
   // round have similar lengths.  Round t gives this CTA tile t * grid + pos,
@@ -176,7 +173,7 @@ __global__ void __launch_bounds__(608, 1)
     const int L = t * (int)gridDim.x + pos;
     if (L >= ntiles) return false;
     int bh, rank;
-    grid_to_tile(L, ntiles / nblk, nblk, kFwdHeadWindow, bh, rank);
+    grid_to_tile(L, ntiles / nblk, nblk, win, bh, rank);
     const int qt = causal ? (nblk - 1 - rank) : rank;
     tl.bh = bh;
     tl.b = bh / H;
@@ -596,10 +593,11 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   const int ntiles = a.B * a.H * ((a.Sq + C::BM - 1) / C::BM);
   const int nsm = sm_count();
   if (nsm <= 0) return FA_ERR_DEVICE;
-  dim3 grid(ntiles < nsm ? ntiles : nsm);  // persistent: one CTA per SM
+  const int g = tile_grid(ntiles, nsm);
+  dim3 grid(g);
   const cudaError_t e = launch_pdl(fa_fwd_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream,
                                    *a.tm_q, *a.tm_k, *a.tm_v, static_cast<T*>(a.o), a.lse,
-                                   a.Sq, a.Sk, a.H, a.H / a.Hkv, ntiles,
+                                   a.Sq, a.Sk, a.H, a.H / a.Hkv, ntiles, tile_window(ntiles, g),
                                    a.scale * 1.4426950408889634f,
                                    a.causal,
                                    a.status, a.timeout_ns, a.debug_flags);

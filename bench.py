@@ -292,7 +292,7 @@ def run_ours(args, wl):
     # down (so not a clock effect; emptying the allocator cache recovered a
     # quarter of the gap).
     headline = None
-    if rank == 0 and world == 1 and wl != "c3b":
+    if rank == 0 and world == 1 and wl != "c3b" and not args.kernels_only:
         hl_clocks = ClockSampler(local)
         hl_clocks.start()
         headline = bench_small("c3b", dev, args)

@@ -464,99 +464,99 @@ __global__ void __launch_bounds__(544, 1)
       bool ok = true;
       int gs = 0, nt = 0;  // iterations and (non-empty) tiles before this one
       for (int t = 0; ok && t < rounds; ++t) {
-       KTile tl;
-       if (!tile_at(t, tl) || tl.nit == 0) continue;
-       if (role != 2 && !mbar_wait(bar(C_KVFULL), (uint32_t)nt & 1u, wc)) break;
-       // the first dV / dK MMAs of a tile overwrite the accumulators: the
-       // previous tile's epilogue must have read them
-       if (role == 2 && nt > 0 && !mbar_wait(bar(C_DKVFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
-       for (int it = 0; it < tl.nit; ++it) {
-        const int gi = gs + it;
-        const int st = gi % C::NST;
-        const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
-        const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
-        if (role <= 1) {
-          // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
-          if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc)) { ok = false; break; }
-          if (role == 0) TRACE(15, gi);
-          if (gi > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(gi - 1) & 1u, wc)) { ok = false; break; }
-          if (role == 0) TRACE(2, gi);
-          if (role == 0 && gi == 0) CTRACE(2);
-          tc_fence_after();
-          const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
-          const uint32_t bbase = role == 0 ? qb : dob;
-          const uint32_t dcol = tmem + (role == 0 ? C::COL_S : C::COL_DP);
+        KTile tl;
+        if (!tile_at(t, tl) || tl.nit == 0) continue;
+        if (role != 2 && !mbar_wait(bar(C_KVFULL), (uint32_t)nt & 1u, wc)) break;
+        // the first dV / dK MMAs of a tile overwrite the accumulators: the
+        // previous tile's epilogue must have read them
+        if (role == 2 && nt > 0 && !mbar_wait(bar(C_DKVFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
+        for (int it = 0; it < tl.nit; ++it) {
+          const int gi = gs + it;
+          const int st = gi % C::NST;
+          const uint32_t qb = sbase + C::OFF_Q + st * C::Q_BYTES;
+          const uint32_t dob = sbase + C::OFF_DO + st * C::Q_BYTES;
+          if (role <= 1) {
+            // S^T (role 0) or dP^T (role 1): M = 128 key rows, N = BM, K = D
+            if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc)) { ok = false; break; }
+            if (role == 0) TRACE(15, gi);
+            if (gi > 0 && !mbar_wait(bar(C_SFREE), (uint32_t)(gi - 1) & 1u, wc)) { ok = false; break; }
+            if (role == 0) TRACE(2, gi);
+            if (role == 0 && gi == 0) CTRACE(2);
+            tc_fence_after();
+            const uint32_t abase = sbase + (role == 0 ? C::OFF_K : C::OFF_V);
+            const uint32_t bbase = role == 0 ? qb : dob;
+            const uint32_t dcol = tmem + (role == 0 ? C::COL_S : C::COL_DP);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int a = (kk * 16) / C::AE;
-            const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
-            const uint64_t ad = make_smem_desc(abase + a * C::BN * C::SWB + koff, 16, 8 * C::SWB, swz);
-            const uint64_t bd = make_smem_desc(bbase + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
-            mma_f16_ss(dcol, ad, bd, id_s, kk > 0 ? 1u : 0u);
-          }
-          // extra K step: + (-LSE/scale) resp. + (-delta) for each query column
-          mma_f16_ss(dcol, make_smem_desc(sbase + C::OFF_ONE, 128, 256, 0),
-                     make_smem_desc(sbase + (role == 0 ? C::OFF_QA : C::OFF_DA) + st * C::AUG_BYTES,
-                                    128, 256, 0),
-                     id_s, 1u);
-          mma_commit(bar(C_SFULL));
-          if (role == 0) TRACE(3, gi);
-        } else if (role == 2) {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc)) { ok = false; break; }
-          TRACE(4, gi);
-          tc_fence_after();
-          // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
-#pragma unroll
-          for (int kk = 0; kk < C::BM / 16; ++kk) {
-            const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-            mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < C::BM / 16; ++kk) {
-            const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
-            if constexpr (C::DS_TMEM) {
-              mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
-                         (it > 0 || kk > 0) ? 1u : 0u);
-            } else {
-              const int a = kk / 4;
-              const uint32_t koff = (uint32_t)(kk % 4) * 32u;
-              const uint64_t sd =
-                  make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
-              mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int a = (kk * 16) / C::AE;
+              const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
+              const uint64_t ad = make_smem_desc(abase + a * C::BN * C::SWB + koff, 16, 8 * C::SWB, swz);
+              const uint64_t bd = make_smem_desc(bbase + a * C::BM * C::SWB + koff, 16, 8 * C::SWB, swz);
+              mma_f16_ss(dcol, ad, bd, id_s, kk > 0 ? 1u : 0u);
             }
-          }
-          mma_commit(bar(C_QEMPTY + st));
-          mma_commit(bar(C_PFREE));
-          TRACE(6, gi);
-        } else {
-          if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc) ||
-              (gi > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(gi - 1) & 1u, wc))) {
-            ok = false;
-            break;
-          }
-          TRACE(5, gi);
-          tc_fence_after();
-          // dQ partial over this key tile (K = 128 key rows)
+            // extra K step: + (-LSE/scale) resp. + (-delta) for each query column
+            mma_f16_ss(dcol, make_smem_desc(sbase + C::OFF_ONE, 128, 256, 0),
+                       make_smem_desc(sbase + (role == 0 ? C::OFF_QA : C::OFF_DA) + st * C::AUG_BYTES,
+                                      128, 256, 0),
+                       id_s, 1u);
+            mma_commit(bar(C_SFULL));
+            if (role == 0) TRACE(3, gi);
+          } else if (role == 2) {
+            if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc)) { ok = false; break; }
+            TRACE(4, gi);
+            tc_fence_after();
+            // dV += P^T dO ; dK += dS^T Q   (M = 128 key rows, N = D, K = BM)
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {
-            const uint64_t dsd =
-                make_smem_desc(sbase + C::OFF_DS + kk * 16 * 128, C::BN * 128, 1024, 2);
-            const uint64_t kd =
-                make_smem_desc(sbase + C::OFF_K + kk * 16 * C::SWB, C::BN * C::SWB, 8 * C::SWB, swz);
-            if constexpr (C::DQT)
-              mma_f16_ss(tmem + C::COL_DQ, kd, dsd, id_dq, kk > 0 ? 1u : 0u);  // K^T dS^T
-            else
-              mma_f16_ss(tmem + C::COL_DQ, dsd, kd, id_dq, kk > 0 ? 1u : 0u);  // dS K
+            for (int kk = 0; kk < C::BM / 16; ++kk) {
+              const uint64_t bd = make_smem_desc(dob + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+              mma_f16_ts(tmem + C::COL_DV, tmem + C::COL_PT + kk * 8, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < C::BM / 16; ++kk) {
+              const uint64_t bd = make_smem_desc(qb + kk * 16 * C::SWB, C::BM * C::SWB, 8 * C::SWB, swz);
+              if constexpr (C::DS_TMEM) {
+                mma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DST + kk * 8, bd, id_kv,
+                           (it > 0 || kk > 0) ? 1u : 0u);
+              } else {
+                const int a = kk / 4;
+                const uint32_t koff = (uint32_t)(kk % 4) * 32u;
+                const uint64_t sd =
+                    make_smem_desc(sbase + C::OFF_DS + a * C::BN * 128 + koff, 16, 1024, 2);
+                mma_f16_ss(tmem + C::COL_DK, sd, bd, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            mma_commit(bar(C_QEMPTY + st));
+            mma_commit(bar(C_PFREE));
+            TRACE(6, gi);
+          } else {
+            if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc) ||
+                (gi > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(gi - 1) & 1u, wc))) {
+              ok = false;
+              break;
+            }
+            TRACE(5, gi);
+            tc_fence_after();
+            // dQ partial over this key tile (K = 128 key rows)
+#pragma unroll
+            for (int kk = 0; kk < C::BN / 16; ++kk) {
+              const uint64_t dsd =
+                  make_smem_desc(sbase + C::OFF_DS + kk * 16 * 128, C::BN * 128, 1024, 2);
+              const uint64_t kd =
+                  make_smem_desc(sbase + C::OFF_K + kk * 16 * C::SWB, C::BN * C::SWB, 8 * C::SWB, swz);
+              if constexpr (C::DQT)
+                mma_f16_ss(tmem + C::COL_DQ, kd, dsd, id_dq, kk > 0 ? 1u : 0u);  // K^T dS^T
+              else
+                mma_f16_ss(tmem + C::COL_DQ, dsd, kd, id_dq, kk > 0 ? 1u : 0u);  // dS K
+            }
+            mma_commit(bar(C_DQFULL));
+            mma_commit(bar(C_PFREE));
           }
-          mma_commit(bar(C_DQFULL));
-          mma_commit(bar(C_PFREE));
         }
-       }
-       if (!ok) break;
-       if (role == 2) mma_commit(bar(C_KVDONE));  // dK / dV of this tile complete
-       else mma_commit(bar(C_KVEMPTY));           // K / V may be reloaded
-       gs += tl.nit;
-       ++nt;
+        if (!ok) break;
+        if (role == 2) mma_commit(bar(C_KVDONE));  // dK / dV of this tile complete
+        else mma_commit(bar(C_KVEMPTY));           // K / V may be reloaded
+        gs += tl.nit;
+        ++nt;
       }
       mma_commit(bar(C_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
@@ -571,153 +571,153 @@ __global__ void __launch_bounds__(544, 1)
     bool ok = true;
     int gs = 0, nt = 0;  // iterations and (non-empty) tiles before this one
     for (int t = 0; ok && t < rounds; ++t) {
-     KTile tl;
-     if (!tile_at(t, tl)) continue;
-     const int kv0 = tl.kv0, nit = tl.nit;
-     const int kv_idx = kv0 + r;
-     const bool kv_ok = kv_idx < Sk;
-     if (nit == 0) {
-       // no query row sees this key tile (Sq < Sk): dK = dV = 0
-       const size_t row_off = (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
-       if (kv_ok && hf * EC < D)
-         for (int c = 0; c < EC; c += 8) {
-           *reinterpret_cast<uint4*>(dv + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
-           *reinterpret_cast<uint4*>(dk + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
-         }
-       continue;
-     }
-     for (int it = 0; it < nit; ++it) {
-      const int gi = gs + it;
-      const int st = gi % C::NST;
-      const int q0 = q_row0(tl, it);
-      if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc) ||
-          !mbar_wait(bar(C_SFULL), (uint32_t)gi & 1u, wc)) {
-        ok = false;
-        break;
+      KTile tl;
+      if (!tile_at(t, tl)) continue;
+      const int kv0 = tl.kv0, nit = tl.nit;
+      const int kv_idx = kv0 + r;
+      const bool kv_ok = kv_idx < Sk;
+      if (nit == 0) {
+         // no query row sees this key tile (Sq < Sk): dK = dV = 0
+         const size_t row_off = (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
+         if (kv_ok && hf * EC < D)
+           for (int c = 0; c < EC; c += 8) {
+             *reinterpret_cast<uint4*>(dv + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
+             *reinterpret_cast<uint4*>(dk + row_off + c) = make_uint4(0u, 0u, 0u, 0u);
+           }
+         continue;
       }
-      if (threadIdx.x == 0) TRACE(7, gi);
-      tc_fence_after();
-      // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
-      // dP^T are released after the last chunk's loads; P^T / dS^T are written only
-      // once the previous tile's dV / dK MMAs have read them (PFREE).
+      for (int it = 0; it < nit; ++it) {
+        const int gi = gs + it;
+        const int st = gi % C::NST;
+        const int q0 = q_row0(tl, it);
+        if (!mbar_wait(bar(C_QFULL + st), (uint32_t)(gi / C::NST) & 1u, wc) ||
+            !mbar_wait(bar(C_SFULL), (uint32_t)gi & 1u, wc)) {
+          ok = false;
+          break;
+        }
+        if (threadIdx.x == 0) TRACE(7, gi);
+        tc_fence_after();
+        // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
+        // dP^T are released after the last chunk's loads; P^T / dS^T are written only
+        // once the previous tile's dV / dK MMAs have read them (PFREE).
 #pragma unroll 1
-      // every (query, key) pair of this tile is unmasked
-      const bool full_tile = (kv0 + C::BN <= Sk) && (!causal || q0 + off >= kv0 + C::BN - 1);
-      for (int cc = 0; cc < HW / 32; ++cc) {
-        const int cb = c0 + cc * 32;  // first query column of this chunk
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
-        tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
-        tmem_wait_ld();
-        if (threadIdx.x == 0 && cc == 0) TRACE(14, gi);
-        if (cc == HW / 32 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(C_SFREE));
-          if (threadIdx.x == 0) TRACE(8, gi);
-        }
-        // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
-        // dP'^T already hold -LSE/scale and -delta).  Only tiles that cross the
-        // causal diagonal or the end of the sequence need the per-element mask.
-        uint32_t pp[16], dd[16];
-        if (full_tile) {
-          const uint64_t c2 = f2_pack(scale_log2, scale_log2);
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            float x0, x1;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2),
-                      x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            float d0, d1;
-            f2_unpack(f2_mul(f2_pack(p0, p1),
-                             f2_pack(__uint_as_float(dr[2 * k]), __uint_as_float(dr[2 * k + 1]))),
-                      d0, d1);
-            pp[k] = Elem<T>::pack2(p0, p1);
-            dd[k] = Elem<T>::pack2(d0, d1);
+        // every (query, key) pair of this tile is unmasked
+        const bool full_tile = (kv0 + C::BN <= Sk) && (!causal || q0 + off >= kv0 + C::BN - 1);
+        for (int cc = 0; cc < HW / 32; ++cc) {
+          const int cb = c0 + cc * 32;  // first query column of this chunk
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
+          tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
+          tmem_wait_ld();
+          if (threadIdx.x == 0 && cc == 0) TRACE(14, gi);
+          if (cc == HW / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(C_SFREE));
+            if (threadIdx.x == 0) TRACE(8, gi);
           }
-        } else {
+          // P^T and dS^T for these 32 query columns, packed to fp16 pairs (S'^T and
+          // dP'^T already hold -LSE/scale and -delta).  Only tiles that cross the
+          // causal diagonal or the end of the sequence need the per-element mask.
+          uint32_t pp[16], dd[16];
+          if (full_tile) {
+            const uint64_t c2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float p4[4], ds4[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int ql = cb + e + u;
-              const bool valid = kv_ok && (!causal || (q0 + ql + off) >= kv_idx);
-              const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
-              p4[u] = pe;
-              ds4[u] = pe * __uint_as_float(dr[e + u]);
+            for (int k = 0; k < 16; ++k) {
+              float x0, x1;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2),
+                        x0, x1);
+              const float p0 = ex2(x0), p1 = ex2(x1);
+              float d0, d1;
+              f2_unpack(f2_mul(f2_pack(p0, p1),
+                               f2_pack(__uint_as_float(dr[2 * k]), __uint_as_float(dr[2 * k + 1]))),
+                        d0, d1);
+              pp[k] = Elem<T>::pack2(p0, p1);
+              dd[k] = Elem<T>::pack2(d0, d1);
             }
-            pp[e / 2] = Elem<T>::pack2(p4[0], p4[1]);
-            pp[e / 2 + 1] = Elem<T>::pack2(p4[2], p4[3]);
-            dd[e / 2] = Elem<T>::pack2(ds4[0], ds4[1]);
-            dd[e / 2 + 1] = Elem<T>::pack2(ds4[2], ds4[3]);
-          }
-        }
-        if (cc == 0) {
-          if (threadIdx.x == 0) TRACE(11, gi);
-          if (gi > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(gi - 1) & 1u, wc)) {
-            ok = false;
-            break;
-          }
-          if (threadIdx.x == 0) TRACE(9, gi);
-        }
-        // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
-        // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
-        tmem_st16(tmem + lane_base + C::COL_PT + cb / 2, pp);
-        if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + cb / 2, dd);
-        const int a = cb / 64;
-        const int ch0 = (cb % 64) / 8;
-        const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+          } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
-                       dd[4 * u + 3]);
+            for (int e = 0; e < 32; e += 4) {
+              float p4[4], ds4[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int ql = cb + e + u;
+                const bool valid = kv_ok && (!causal || (q0 + ql + off) >= kv_idx);
+                const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * scale_log2) : 0.f;
+                p4[u] = pe;
+                ds4[u] = pe * __uint_as_float(dr[e + u]);
+              }
+              pp[e / 2] = Elem<T>::pack2(p4[0], p4[1]);
+              pp[e / 2 + 1] = Elem<T>::pack2(p4[2], p4[3]);
+              dd[e / 2] = Elem<T>::pack2(ds4[0], ds4[1]);
+              dd[e / 2 + 1] = Elem<T>::pack2(ds4[2], ds4[3]);
+            }
+          }
+          if (cc == 0) {
+            if (threadIdx.x == 0) TRACE(11, gi);
+            if (gi > 0 && !mbar_wait(bar(C_PFREE), (uint32_t)(gi - 1) & 1u, wc)) {
+              ok = false;
+              break;
+            }
+            if (threadIdx.x == 0) TRACE(9, gi);
+          }
+          // P^T (and for D=128 dS^T) into tensor memory; dS^T into the [key row][query
+          // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
+          tmem_st16(tmem + lane_base + C::COL_PT + cb / 2, pp);
+          if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + cb / 2, dd);
+          const int a = cb / 64;
+          const int ch0 = (cb % 64) / 8;
+          const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
+                         dd[4 * u + 3]);
+        }
+        if (!ok) break;
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C_DSREADY));
+        if (threadIdx.x == 0) TRACE(10, gi);
       }
       if (!ok) break;
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(C_DSREADY));
-      if (threadIdx.x == 0) TRACE(10, gi);
-     }
-     if (!ok) break;
-     // ---------------------------------------------------------- dK / dV epilogue
-     if (!mbar_wait(bar(C_KVDONE), (uint32_t)nt & 1u, wc)) { ok = false; break; }
-     tc_fence_after();
-     if (hf * EC < D) {
+      // ---------------------------------------------------------- dK / dV epilogue
+      if (!mbar_wait(bar(C_KVDONE), (uint32_t)nt & 1u, wc)) { ok = false; break; }
+      tc_fence_after();
+      if (hf * EC < D) {
 #pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
-        const float f = pass == 0 ? 1.f : scale;
-        T* dst = (pass == 0 ? dv : dk) + (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
+        for (int pass = 0; pass < 2; ++pass) {
+          const uint32_t col = (pass == 0 ? C::COL_DV : C::COL_DK) + hf * EC;
+          const float f = pass == 0 ? 1.f : scale;
+          T* dst = (pass == 0 ? dv : dk) + (((size_t)tl.b * Sk + kv_idx) * Hkv + tl.hk) * D + hf * EC;
 #pragma unroll
-        for (int c = 0; c < EC / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld16(tmem + lane_base + col + c * 16, v);
-          tmem_wait_ld();
-          uint4 w0, w1;
-          w0.x = Elem<T>::pack2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
-          w0.y = Elem<T>::pack2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
-          w0.z = Elem<T>::pack2(__uint_as_float(v[4]) * f, __uint_as_float(v[5]) * f);
-          w0.w = Elem<T>::pack2(__uint_as_float(v[6]) * f, __uint_as_float(v[7]) * f);
-          w1.x = Elem<T>::pack2(__uint_as_float(v[8]) * f, __uint_as_float(v[9]) * f);
-          w1.y = Elem<T>::pack2(__uint_as_float(v[10]) * f, __uint_as_float(v[11]) * f);
-          w1.z = Elem<T>::pack2(__uint_as_float(v[12]) * f, __uint_as_float(v[13]) * f);
-          w1.w = Elem<T>::pack2(__uint_as_float(v[14]) * f, __uint_as_float(v[15]) * f);
-          if (kv_ok) {
-            reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
-            reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
+          for (int c = 0; c < EC / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + col + c * 16, v);
+            tmem_wait_ld();
+            uint4 w0, w1;
+            w0.x = Elem<T>::pack2(__uint_as_float(v[0]) * f, __uint_as_float(v[1]) * f);
+            w0.y = Elem<T>::pack2(__uint_as_float(v[2]) * f, __uint_as_float(v[3]) * f);
+            w0.z = Elem<T>::pack2(__uint_as_float(v[4]) * f, __uint_as_float(v[5]) * f);
+            w0.w = Elem<T>::pack2(__uint_as_float(v[6]) * f, __uint_as_float(v[7]) * f);
+            w1.x = Elem<T>::pack2(__uint_as_float(v[8]) * f, __uint_as_float(v[9]) * f);
+            w1.y = Elem<T>::pack2(__uint_as_float(v[10]) * f, __uint_as_float(v[11]) * f);
+            w1.z = Elem<T>::pack2(__uint_as_float(v[12]) * f, __uint_as_float(v[13]) * f);
+            w1.w = Elem<T>::pack2(__uint_as_float(v[14]) * f, __uint_as_float(v[15]) * f);
+            if (kv_ok) {
+              reinterpret_cast<uint4*>(dst + c * 16)[0] = w0;
+              reinterpret_cast<uint4*>(dst + c * 16)[1] = w1;
+            }
           }
         }
       }
-     }
-     // dK / dV have been read: the next tile's first dV / dK MMAs may overwrite them
-     tc_fence_before();
-     __syncwarp();
-     if (lane == 0) mbar_arrive(bar(C_DKVFREE));
-     gs += nit;
-     ++nt;
+      // dK / dV have been read: the next tile's first dV / dK MMAs may overwrite them
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_DKVFREE));
+      gs += nit;
+      ++nt;
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------ dQ epilogue warps 8..11
@@ -729,78 +729,78 @@ __global__ void __launch_bounds__(544, 1)
     bool ok = true;
     int gs = 0;  // iterations of the earlier tiles
     for (int t = 0; ok && t < rounds; ++t) {
-     KTile tl;
-     if (!tile_at(t, tl) || tl.nit == 0) continue;
-     for (int it = 0; it < tl.nit; ++it) {
-      const int gi = gs + it;
-      const int q0 = q_row0(tl, it);
-      const int bh = tl.b * H + q_head(tl, it);
-      const int sbuf = gi % C::NDQ;
-      const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
-      if (!mbar_wait(bar(C_DQFULL), (uint32_t)gi & 1u, wc)) { ok = false; break; }
-      if (tid == 0) TRACE(12, gi);
-      tc_fence_after();
-      if constexpr (C::DQT) {
-        // TMEM lane = d, column = query row
-        const int d = wq * 32 + lane;
-        uint32_t v0[32], v1[32];
-        tmem_ld32(tmem + lane_base + C::COL_DQ, v0);
-        tmem_ld32(tmem + lane_base + C::COL_DQ + 32, v1);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(C_DQFREE));
-        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
-        named_bar_sync(1, 128);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) st_shared_f32(stage + (uint32_t)(e * D + d) * 4u, __uint_as_float(v0[e]));
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          st_shared_f32(stage + (uint32_t)((32 + e) * D + d) * 4u, __uint_as_float(v1[e]));
-      } else {
-        // TMEM lane = query row, column = d; CW columns at a time (flat register
-        // use). The staging buffer must be free before the first chunk's stores;
-        // the accumulator is released after the last chunk's loads.
-        constexpr int CW = D < 32 ? D : 32;
-        constexpr int NP = CW / 4;  // 16-byte pieces per chunk row
-        const int qr = wq * 32 + lane;
-        if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
-        named_bar_sync(1, 128);
-        const uint32_t rowa = stage + (uint32_t)(qr * D * 4);
-#pragma unroll
-        for (int c = 0; c < D / CW; ++c) {
-          uint32_t v[CW];
-          if constexpr (CW == 32)
-            tmem_ld32(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[32]>(v));
-          else
-            tmem_ld16(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[16]>(v));
+      KTile tl;
+      if (!tile_at(t, tl) || tl.nit == 0) continue;
+      for (int it = 0; it < tl.nit; ++it) {
+        const int gi = gs + it;
+        const int q0 = q_row0(tl, it);
+        const int bh = tl.b * H + q_head(tl, it);
+        const int sbuf = gi % C::NDQ;
+        const uint32_t stage = sbase + C::OFF_DQS + sbuf * C::DQ_STAGE_BYTES;
+        if (!mbar_wait(bar(C_DQFULL), (uint32_t)gi & 1u, wc)) { ok = false; break; }
+        if (tid == 0) TRACE(12, gi);
+        tc_fence_after();
+        if constexpr (C::DQT) {
+          // TMEM lane = d, column = query row
+          const int d = wq * 32 + lane;
+          uint32_t v0[32], v1[32];
+          tmem_ld32(tmem + lane_base + C::COL_DQ, v0);
+          tmem_ld32(tmem + lane_base + C::COL_DQ + 32, v1);
           tmem_wait_ld();
-          if (c == D / CW - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(C_DQFREE));
-          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_DQFREE));
+          if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
+          named_bar_sync(1, 128);
 #pragma unroll
-          for (int p = 0; p < NP; ++p) {
-            const int pc = (p + lane) % NP;  // rotate pieces across lanes: fewer bank conflicts
-            uint32_t w0 = v[0], w1 = v[1], w2 = v[2], w3 = v[3];
-            // select the rotated piece without dynamic register indexing
+          for (int e = 0; e < 32; ++e) st_shared_f32(stage + (uint32_t)(e * D + d) * 4u, __uint_as_float(v0[e]));
 #pragma unroll
-            for (int t = 0; t < NP; ++t)
-              if (t == pc) { w0 = v[4 * t]; w1 = v[4 * t + 1]; w2 = v[4 * t + 2]; w3 = v[4 * t + 3]; }
-            st_shared_v4(rowa + (uint32_t)(c * CW + 4 * pc) * 4u, w0, w1, w2, w3);
+          for (int e = 0; e < 32; ++e)
+            st_shared_f32(stage + (uint32_t)((32 + e) * D + d) * 4u, __uint_as_float(v1[e]));
+        } else {
+          // TMEM lane = query row, column = d; CW columns at a time (flat register
+          // use). The staging buffer must be free before the first chunk's stores;
+          // the accumulator is released after the last chunk's loads.
+          constexpr int CW = D < 32 ? D : 32;
+          constexpr int NP = CW / 4;  // 16-byte pieces per chunk row
+          const int qr = wq * 32 + lane;
+          if (tid == 0) bulk_wait_group_read<C::NDQ - 1>();  // this buffer's last reduction read it
+          named_bar_sync(1, 128);
+          const uint32_t rowa = stage + (uint32_t)(qr * D * 4);
+#pragma unroll
+          for (int c = 0; c < D / CW; ++c) {
+            uint32_t v[CW];
+            if constexpr (CW == 32)
+              tmem_ld32(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[32]>(v));
+            else
+              tmem_ld16(tmem + lane_base + C::COL_DQ + c * CW, *reinterpret_cast<uint32_t(*)[16]>(v));
+            tmem_wait_ld();
+            if (c == D / CW - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar(C_DQFREE));
+            }
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+              const int pc = (p + lane) % NP;  // rotate pieces across lanes: fewer bank conflicts
+              uint32_t w0 = v[0], w1 = v[1], w2 = v[2], w3 = v[3];
+              // select the rotated piece without dynamic register indexing
+#pragma unroll
+              for (int t = 0; t < NP; ++t)
+                if (t == pc) { w0 = v[4 * t]; w1 = v[4 * t + 1]; w2 = v[4 * t + 2]; w3 = v[4 * t + 3]; }
+              st_shared_v4(rowa + (uint32_t)(c * CW + 4 * pc) * 4u, w0, w1, w2, w3);
+            }
           }
         }
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (tid == 0) {
+          bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
+          bulk_commit_group();
+          TRACE(13, gi);
+        }
       }
-      fence_proxy_async_smem();
-      named_bar_sync(1, 128);
-      if (tid == 0) {
-        bulk_reduce_add_f32(dq_acc + ((size_t)bh * S_pad + q0) * D, stage, C::DQ_STAGE_BYTES);
-        bulk_commit_group();
-        TRACE(13, gi);
-      }
-     }
-     gs += tl.nit;
+      gs += tl.nit;
     }
     if (tid == 0) bulk_wait_group_all();
   }

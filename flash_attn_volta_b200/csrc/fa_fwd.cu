@@ -294,38 +294,38 @@ __global__ void __launch_bounds__(608, 1)
       bool ok = true;
       int gs = 0, nq = 0;
       for (int t = 0; ok && t < rounds; ++t) {
-       Tile tl;
-       if (!tile_at(t, tl) || tl.nkv == 0) continue;
-       if (!mbar_wait(bar(B_QFULL), (uint32_t)nq & 1u, wc)) break;
-       for (int j = 0; j < tl.nkv; ++j) {
-        const int g = gs + j, sk = g % C::NSTK, sb = g & 1;
-        if (!mbar_wait(bar(B_KFULL + sk), (uint32_t)(g / C::NSTK) & 1u, wc) ||
-            (g >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((g - 2) >> 1) & 1u, wc))) {
-          ok = false;
-          break;
-        }
-        FTRACE(0, g);
-        if (g == 0) CTRACE(2);
-        tc_fence_after();
+        Tile tl;
+        if (!tile_at(t, tl) || tl.nkv == 0) continue;
+        if (!mbar_wait(bar(B_QFULL), (uint32_t)nq & 1u, wc)) break;
+        for (int j = 0; j < tl.nkv; ++j) {
+          const int g = gs + j, sk = g % C::NSTK, sb = g & 1;
+          if (!mbar_wait(bar(B_KFULL + sk), (uint32_t)(g / C::NSTK) & 1u, wc) ||
+              (g >= 2 && !mbar_wait(bar(B_SFREE + sb), (uint32_t)((g - 2) >> 1) & 1u, wc))) {
+            ok = false;
+            break;
+          }
+          FTRACE(0, g);
+          if (g == 0) CTRACE(2);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int a = (kk * 16) / C::AE;
-          const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
-          const uint64_t ad = make_smem_desc(sbase + C::OFF_Q + a * C::BM * C::SWB + koff, 16,
-                                             8 * C::SWB, swz);
-          const uint64_t bd =
-              make_smem_desc(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB + koff, 16,
-                             8 * C::SWB, swz);
-          mma_f16_ss(tmem + C::COL_S + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int a = (kk * 16) / C::AE;
+            const uint32_t koff = (uint32_t)((kk * 16) % C::AE) * 2u;
+            const uint64_t ad = make_smem_desc(sbase + C::OFF_Q + a * C::BM * C::SWB + koff, 16,
+                                               8 * C::SWB, swz);
+            const uint64_t bd =
+                make_smem_desc(sbase + C::OFF_K + sk * C::KV_BYTES + a * C::BN * C::SWB + koff, 16,
+                               8 * C::SWB, swz);
+            mma_f16_ss(tmem + C::COL_S + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(B_SFULL + sb));
+          mma_commit(bar(B_KEMPTY + sk));
+          FTRACE(1, g);
         }
-        mma_commit(bar(B_SFULL + sb));
-        mma_commit(bar(B_KEMPTY + sk));
-        FTRACE(1, g);
-       }
-       if (!ok) break;
-       mma_commit(bar(B_QEMPTY));  // Q may be reloaded for the next tile
-       ++nq;
-       gs += tl.nkv;
+        if (!ok) break;
+        mma_commit(bar(B_QEMPTY));  // Q may be reloaded for the next tile
+        ++nq;
+        gs += tl.nkv;
       }
       mma_commit(bar(B_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
@@ -337,33 +337,33 @@ __global__ void __launch_bounds__(608, 1)
       bool ok = true;
       int gs = 0, nt = 0;
       for (int t = 0; ok && t < rounds; ++t) {
-       Tile tl;
-       if (!tile_at(t, tl) || tl.nkv == 0) continue;
-       // the first O += P V of a tile overwrites O: the previous epilogue must have read it
-       if (nt > 0 && !mbar_wait(bar(B_OFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
-       for (int j = 0; j < tl.nkv; ++j) {
-        const int g = gs + j, sv = g % C::NSTV, pb = g & 1;
-        if (!mbar_wait(bar(B_PFULL + pb), (uint32_t)(g >> 1) & 1u, wc) ||
-            !mbar_wait(bar(B_VFULL + sv), (uint32_t)(g / C::NSTV) & 1u, wc)) {
-          ok = false;
-          break;
-        }
-        FTRACE(2, g);
-        tc_fence_after();
+        Tile tl;
+        if (!tile_at(t, tl) || tl.nkv == 0) continue;
+        // the first O += P V of a tile overwrites O: the previous epilogue must have read it
+        if (nt > 0 && !mbar_wait(bar(B_OFREE), (uint32_t)(nt - 1) & 1u, wc)) break;
+        for (int j = 0; j < tl.nkv; ++j) {
+          const int g = gs + j, sv = g % C::NSTV, pb = g & 1;
+          if (!mbar_wait(bar(B_PFULL + pb), (uint32_t)(g >> 1) & 1u, wc) ||
+              !mbar_wait(bar(B_VFULL + sv), (uint32_t)(g / C::NSTV) & 1u, wc)) {
+            ok = false;
+            break;
+          }
+          FTRACE(2, g);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t bd = make_smem_desc(sbase + C::OFF_V + sv * C::KV_BYTES + kk * 16 * C::SWB,
-                                             C::BN * C::SWB, 8 * C::SWB, swz);
-          mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + pb * 64 + kk * 8, bd, idesc_pv,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < C::BN / 16; ++kk) {
+            const uint64_t bd = make_smem_desc(sbase + C::OFF_V + sv * C::KV_BYTES + kk * 16 * C::SWB,
+                                               C::BN * C::SWB, 8 * C::SWB, swz);
+            mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + pb * 64 + kk * 8, bd, idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(B_ODONE));
+          mma_commit(bar(B_VEMPTY + sv));
+          mma_commit(bar(B_PFREE + pb));
+          FTRACE(3, g);
         }
-        mma_commit(bar(B_ODONE));
-        mma_commit(bar(B_VEMPTY + sv));
-        mma_commit(bar(B_PFREE + pb));
-        FTRACE(3, g);
-       }
-       ++nt;
-       gs += tl.nkv;
+        ++nt;
+        gs += tl.nkv;
       }
       mma_commit(bar(B_DRAIN));
     }

@@ -57,9 +57,12 @@ WORKLOADS = {
 L2_BYTES = 126 * 1000 * 1000
 
 
-# DRAM bytes (read + write) per launch of the main backward kernel: one ncu
-# capture of the p8k workload (1/16 of c4's (batch, head) pairs), scaled by 16.
-BWD_TRAFFIC_PER_LAUNCH = {"c4": 5.02e9}
+# DRAM bytes (read + write) per launch of the main backward kernel over the
+# workload's whole batch, from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
+# and where it came from; the summaries are under profiles/.
+BWD_TRAFFIC_PER_LAUNCH = {
+    "c4": (5.02e9, "ncu, one launch of the p8k case (1/16 of c4's (batch, head) pairs) x 16"),
+}
 
 
 def flops_fwd(B, S, H, D, causal):
@@ -298,6 +301,8 @@ def run_ours(args, wl):
         headline = bench_small("c3b", dev, args)
         headline["c3a"] = bench_small("c3a", dev, args)
         headline["clocks"] = hl_clocks.stop()
+    mem_c3a = peak_mem_fwd_bwd(dev, 1, 4096, 16, 64, True)
+    torch.cuda.empty_cache()
     b0, b1 = rank * B // world, (rank + 1) * B // world
     q, k, v, do = gen_shard(b0, b1, S, H, D, amp, dev)
     q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
@@ -308,10 +313,26 @@ def run_ours(args, wl):
         out = flash_attn(q, k, v, causal=causal)
         out.backward(do)
 
+    torch.cuda.synchronize(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+    mem0 = torch.cuda.memory_allocated(dev)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
     check_status(dev)
+    # extra device memory of one step beyond its inputs (the output, LSE, the
+    # gradients and the backward's workspace), the reference's bench/memory.py metric
+    step_peak_mib = (torch.cuda.max_memory_allocated(dev) - mem0) / 2**20
+    # power soak: untimed steps until the GPU has run this load for
+    # --soak-s seconds, so every GPU count is timed in the same (power-capped)
+    # state instead of a short burst at boost clocks
+    soak_steps = 0
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak_s:
+        for _ in range(4):
+            step()
+        torch.cuda.synchronize(dev)
+        soak_steps += 4
 
     clocks = ClockSampler(local) if rank == 0 else None
     tensor_bytes = q.numel() * q.element_size()
@@ -438,41 +459,49 @@ def run_ours(args, wl):
             _lib.check(rc, "fa_sm100_bwd_phase")
 
         phase(0)
-        reps = max(3, min(args.steps, 10))
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(reps)]
-        phase(1)
-        for e0, e1 in ev:
-            e0.record(stream)
-            phase(1)
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
-        k_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+        reps = max(5, min(args.steps, 11))
 
-        def time_phase(p):
+        def timed_median(fn):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
             for e0, e1 in ev:
                 e0.record(stream)
-                phase(p)
+                fn()
                 e1.record(stream)
             torch.cuda.synchronize(dev)
-            return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+            return statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+
+        phase(1)
+        k_ms = timed_median(lambda: phase(1))
+
+        def time_phase(p):
+            return timed_median(lambda: phase(p))
 
         pre_ms, post_ms = time_phase(0), time_phase(2)
-        # forward kernel alone, same method
-        evf = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(reps)]
-        for e0, e1 in evf:
-            e0.record(stream)
-            flash_attn_forward(qq, kk_, vv, causal=causal)
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
-        f_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evf)
+        # forward kernel alone: the C ABI on preallocated outputs (no allocation
+        # or Python work inside the event window), median of the launches
+        o_f = torch.empty_like(qq)
+        lse_f = torch.empty((Bl, H, S), dtype=torch.float32, device=dev)
+
+        def fwd_launch():
+            rc = lib.fa_sm100_fwd(qq.data_ptr(), kk_.data_ptr(), vv.data_ptr(), o_f.data_ptr(),
+                                  lse_f.data_ptr(), Bl, S, H, D, scale, 1 if causal else 0,
+                                  status.data_ptr(), _stream_ptr(dev))
+            _lib.check(rc, "fa_sm100_fwd")
+
+        fwd_launch()
+        f_ms = timed_median(fwd_launch)
         check_status(dev)
         del ws
     peak_burst, peak_sus, peak_kind = load_peaks()
     bwd_alg = 2.5 * flops_fwd(Bl, S, H, D, causal)      # 5 GEMMs of the backward
     fwd_alg = flops_fwd(Bl, S, H, D, causal)            # 2 GEMMs of the forward
     k_tflops = bwd_alg / (k_ms * 1e-3) / 1e12
+    traffic, traffic_note = None, "not measured for this workload"
+    if wl in BWD_TRAFFIC_PER_LAUNCH:
+        t_full, src = BWD_TRAFFIC_PER_LAUNCH[wl]
+        traffic = t_full * Bl / B  # this rank's launch covers Bl of the B batches
+        traffic_note = src + (f"; x {Bl}/{B} for this rank's batch shard" if Bl != B else "")
     f_tflops = fwd_alg / (f_ms * 1e-3) / 1e12
 
     cpu = None
@@ -489,9 +518,17 @@ def run_ours(args, wl):
                        "global_batch": B, "seq_len": S, "parallelism": f"batch-shard{world}",
                        "flops_per_step": 2.5 * flops_fwd(B, S, H, D, causal),
                        "flop_convention": "4*B*H*S^2*D (/2 causal), fwd+bwd = 2.5x",
-                       "l2": l2_note},
-            "pct_of_peak": {"value": value / (peak_sus if peak_sus else peak_burst),
-                            "peak_tflops": peak_sus, "kind": f"{peak_kind} bf16 sustained"},
+                       "l2": l2_note, "power_soak": {"seconds": args.soak_s,
+                                                     "untimed_steps": soak_steps}},
+            "memory": {"step_peak_extra_mib_per_gpu": step_peak_mib,
+                       "inputs_mib_per_gpu": 4 * tensor_bytes / 2**20,
+                       "what": "max_memory_allocated during fwd+bwd minus the memory held "
+                               "before it (q, k, v, dO); includes O, LSE, dQ/dK/dV and "
+                               "the backward workspace",
+                       "causal_1x4096x16x64_mib": mem_c3a},
+            "pct_of_peak": {"value": value / (world * (peak_sus if peak_sus else peak_burst)),
+                            "peak_tflops": world * peak_sus,
+                            "kind": f"{peak_kind} bf16 sustained x n_gpus"},
             "gpu_launches": 4 * args.steps,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nb,
                     "d2h_bytes_per_step": 4 * nb, "steps": e2e_steps,
@@ -500,10 +537,11 @@ def run_ours(args, wl):
             "roofline": {"bound": "tensor", "kernel": f"fa_bwd_main_kernel<{D}>",
                          "achieved": k_tflops, "peak": peak_burst, "unit": "TFLOP/s",
                          "frac": k_tflops / peak_burst,
-                         "traffic": BWD_TRAFFIC_PER_LAUNCH.get(wl) if world == 1 else None,
+                         "traffic": traffic,
                          "peak_kind": f"{peak_kind} bf16 burst",
-                         "flops_per_launch": bwd_alg, "mean_ms": k_ms,
-                         "fwd_kernel": {"achieved": f_tflops, "mean_ms": f_ms,
+                         "flops_per_launch": bwd_alg, "median_ms": k_ms,
+                         "traffic_note": traffic_note,
+                         "fwd_kernel": {"achieved": f_tflops, "median_ms": f_ms,
                                         "frac": f_tflops / peak_burst},
                          "bwd_pre_ms": pre_ms, "bwd_post_ms": post_ms},
             "clocks": clock_info,
@@ -516,6 +554,27 @@ def run_ours(args, wl):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def peak_mem_fwd_bwd(dev, B, N, H, D, causal):
+    """Peak extra allocator memory (MiB) of one fwd+bwd step over the memory held
+    before it (q, k, v, dO), measured like the reference's bench/backward.py:69-85
+    (one warm step, reset the peak, forward + backward, max_memory_allocated -
+    memory_allocated before)."""
+    from flash_attn_volta_b200 import flash_attn
+    q, k, v, do = gen_shard(0, B, N, H, D, 1.0, dev, seed_base=99)
+    for t in (q, k, v):
+        t.requires_grad_()
+    flash_attn(q, k, v, causal=causal).backward(do)
+    q.grad = k.grad = v.grad = None
+    torch.cuda.synchronize(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+    base = torch.cuda.memory_allocated(dev)
+    flash_attn(q, k, v, causal=causal).backward(do)
+    torch.cuda.synchronize(dev)
+    peak = torch.cuda.max_memory_allocated(dev) - base
+    del q, k, v, do
+    return peak / 2**20
 
 
 def bench_small(wl, dev, args):
@@ -751,6 +810,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5", "c5long"], default="c4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--soak-s", type=float, default=1.0,
+                    help="seconds of untimed steps between the warm-up and the timed steps")
     ap.add_argument("--kernels-only", action="store_true",
                     help="run only the warm-up and timed steps (for ncu launch lists)")
     args = ap.parse_args()

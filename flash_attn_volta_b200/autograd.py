@@ -39,14 +39,13 @@ class _FlashAttnFn(torch.autograd.Function):
 
 def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                causal: bool = False, sm_scale: float | None = None) -> torch.Tensor:
-    """Autograd-aware FlashAttention on B200.
+    """Attention with gradients: the B200 forward, and the B200 backward when
+    autograd reaches it.
 
-    Args:
-        q, k, v: (B, N, H, D) fp16 on CUDA. D in {16, 32, 64, 128}.
-        causal:  lower-triangular (top-left) mask if True.
-        sm_scale: softmax scale (default 1/sqrt(D)).
-
-    Returns:
-        out: (B, N, H, D) fp16, with autograd hooked up.
+    q, k, v are (batch, seqlen, heads, head_dim) CUDA tensors in fp16 (or bf16),
+    head_dim one of 16, 32, 64, 128.  With ``causal`` each query attends only
+    to keys at or before its own position.  ``sm_scale`` multiplies the scores
+    before the softmax and defaults to head_dim ** -0.5.  The result has q's
+    shape and dtype.
     """
     return _FlashAttnFn.apply(q, k, v, causal, sm_scale)

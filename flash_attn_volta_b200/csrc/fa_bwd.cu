@@ -152,19 +152,40 @@ __host__ __device__ constexpr uint32_t aug_offset(uint32_t row, uint32_t k) {
   return (row / 8) * 256 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2;
 }
 
-// x as three terms of the element type, t0 + t1 + t2 == x to ~2^-22 |x| for fp16
-// and ~2^-24 |x| for bf16 (t0 clamped to the fp16 range; a non-finite x, i.e. a
-// fully masked row, becomes a large negative term that drives every P of the
-// row to zero); returned as the first 16-byte half of an extra-K-step row,
-// [t0, t1, t2, 0, 0, 0, 0, 0].
+// x as four terms of the element type, [t0, t1, t2, a] with
+// t0 + t1 + t2 + kAugBig * a == x (the K / V side of the extra K step holds
+// [1, 1, 1, kAugBig]), exact to ~2^-22 |x| for fp16 and ~2^-24 |x| for bf16.
+// `a` is used only when |x| exceeds the fp16 range of t0 (a delta of a
+// loss-scaled dO, very large logits): a = fp16(x / kAugBig) and the three terms
+// split the remainder, |x - kAugBig * a| <= 2^15, so fp16 covers |x| up to
+// kAugBig * 65504 ~ 1.3e8 exactly.  bf16 has the range for t0 itself and
+// keeps a = 0.  A non-finite x (the +inf LSE of a fully masked row) becomes a
+// large negative sum that drives every P of the row to zero.  A finite x
+// beyond the range is clamped and reported with kStatusRange.  Returned as the
+// first 16-byte half of an extra-K-step row, [t0, t1, t2, a, 0, 0, 0, 0].
 template <typename T>
-__device__ __forceinline__ uint4 split_row(float x) {
-  if (!(fabsf(x) <= 60000.f)) x = (x > 0.f) ? 60000.f : -60000.f;
+__device__ __forceinline__ uint4 split_row(float x, int* status) {
+  uint16_t ba = 0;
+  if (std::is_same<T, __half>::value) {
+    constexpr float kLim = (float)kAugBig * 65504.f;
+    if (!(fabsf(x) <= kLim)) {
+      if (status && fabsf(x) != __int_as_float(0x7f800000) && x == x) atomicOr(status, kStatusRange);
+      x = (x > 0.f) ? kLim : -kLim;
+    }
+    if (fabsf(x) > 60000.f) {
+      ba = Elem<T>::bits(x * (1.0f / (float)kAugBig));
+      x -= (float)kAugBig * Elem<T>::value(ba);  // exact: both are multiples of ulp(x)
+    }
+  } else if (!(fabsf(x) <= Elem<T>::kMax)) {
+    if (status && fabsf(x) != __int_as_float(0x7f800000) && x == x) atomicOr(status, kStatusRange);
+    x = (x > 0.f) ? Elem<T>::kMax : -Elem<T>::kMax;
+  }
   const uint16_t b0 = Elem<T>::bits(x);
   const float r1 = x - Elem<T>::value(b0);
   const uint16_t b1 = Elem<T>::bits(r1);
   const uint16_t b2 = Elem<T>::bits(r1 - Elem<T>::value(b1));
-  return make_uint4((uint32_t)b0 | ((uint32_t)b1 << 16), (uint32_t)b2, 0u, 0u);
+  return make_uint4((uint32_t)b0 | ((uint32_t)b1 << 16), (uint32_t)b2 | ((uint32_t)ba << 16), 0u,
+                    0u);
 }
 
 // D/8 threads per (bh, row) of the padded row range, 16-byte loads of O and dO:
@@ -176,7 +197,7 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const T* __restrict__ o, const T* __restrict__ dout, const float* __restrict__ lse,
     uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc,
     int S /* query rows */,
-    int H, int D, int S_pad, float inv_scale) {
+    int H, int D, int S_pad, float inv_scale, int* status) {
   griddep_wait();  // O and LSE come from the forward
   griddep_launch_dependents();
   const int tpr = D / 8;  // threads per row: 2, 4, 8 or 16 (a power of two inside a warp)
@@ -208,9 +229,9 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     // row blocks of S_pad rows per (batch, head); S_pad is a multiple of 8
     const size_t base = (size_t)bh * S_pad * kAugRowBytes;
     const uint32_t r = (uint32_t)row;
-    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 0)) = split_row<T>(-l * inv_scale);
+    *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 0)) = split_row<T>(-l * inv_scale, status);
     *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) = split_row<T>(-acc);
+    *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) = split_row<T>(-acc, status);
     *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
   }
   float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
@@ -339,10 +360,10 @@ __global__ void __launch_bounds__(544, 1)
     tmem_relinquish();
   }
   if (warp >= 8 && warp < 12) {
-    // the extra K-step rows of K and V: [1, 1, 1, 0, ...] for each of the 128 key rows
+    // the extra K-step rows of K and V: [1, 1, 1, kAugBig, 0, ...] for each of the 128 key rows
     const uint32_t r = threadIdx.x - 256;
     st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 0), Elem<T>::kOne | (Elem<T>::kOne << 16),
-                 Elem<T>::kOne, 0u, 0u);
+                 Elem<T>::kOne | ((uint32_t)Elem<T>::bits((float)kAugBig) << 16), 0u, 0u);
     st_shared_v4(sbase + C::OFF_ONE + aug_offset(r, 8), 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
   }
@@ -597,10 +618,9 @@ __global__ void __launch_bounds__(544, 1)
         }
         if (threadIdx.x == 0) TRACE(7, gi);
         tc_fence_after();
-        // 32 query columns at a time (keeps register use flat for BM = 128). S^T and
+        // 32 query columns at a time (bounds the registers held for BM = 128). S^T and
         // dP^T are released after the last chunk's loads; P^T / dS^T are written only
         // once the previous tile's dV / dK MMAs have read them (PFREE).
-#pragma unroll 1
         // every (query, key) pair of this tile is unmasked
         const bool full_tile = (kv0 + C::BN <= Sk) && (!causal || q0 + off >= kv0 + C::BN - 1);
         for (int cc = 0; cc < HW / 32; ++cc) {
@@ -848,7 +868,7 @@ static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream, int phase) {
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
     if (launch_pdl(fa_bwd_pre_kernel<T>, grid, dim3(256), 0, stream, static_cast<const T*>(a.o),
                    static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.Sq, a.H,
-                   a.D, a.S_pad, 1.0f / a.scale) != cudaSuccess)
+                   a.D, a.S_pad, 1.0f / a.scale, a.status) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   int rc = FA_OK;

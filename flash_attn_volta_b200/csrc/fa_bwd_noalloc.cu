@@ -12,7 +12,9 @@
 // The array's name is only a host-side stand-in in host code, so its device
 // address is looked up with cudaGetSymbolAddress, once per device, with that
 // device current, on the first call made on that device.  Make that first call
-// before any stream capture.  Every call shares the one array: the kernels
+// before any stream capture.  The address is kept for the life of the process,
+// so a device or primary-context reset (cudaDeviceReset) after that first call
+// is not supported: the kept address would belong to the destroyed context.  Every call shares the one array: the kernels
 // rewrite and re-zero the part they use on each call, and two calls whose
 // kernels overlap on the GPU (different streams, or different host threads)
 // race on it and give wrong results.

@@ -125,6 +125,9 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 // Bytes of one row of the augmented K step (16 fp16).
 constexpr int kAugRowBytes = 32;
+// Weight of the fourth row term of the augmented K step (a power of two, exact
+// in fp16 and bf16): the K / V side holds [1, 1, 1, kAugBig, 0, ...].
+constexpr int kAugBig = 2048;
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 // phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion

@@ -29,6 +29,7 @@ namespace fa_sm100 {
 enum : int {
   kStatusOk = 0,
   kStatusTimeout = 1,   // a bounded mbarrier wait ran out
+  kStatusRange = 2,     // a backward row term (LSE / scale or delta) beyond the representable range
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

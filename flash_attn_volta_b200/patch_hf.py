@@ -185,21 +185,24 @@ def unpatch_llama(model: torch.nn.Module) -> int:
 
 # Linear-attention / state-space models (patch_hf.py:353-387 of the reference):
 # the kernel computes softmax attention only, so patch_model refuses these.
+# Module class name -> the family reported in the refusal.
+_NON_SOFTMAX_MIXERS = {
+    "MambaMixer": "mamba",
+    "Mamba2Mixer": "mamba2",
+    "RwkvSelfAttention": "rwkv",
+    "RwkvLinearAttention": "rwkv",
+    "RecurrentGemmaRecurrentBlock": "recurrent_gemma",
+    "RetNetAttention": "retnet",
+}
+
+
 def _linear_attn_family(model: torch.nn.Module) -> Optional[str]:
     """Family name (mamba / mamba2 / rwkv / recurrent_gemma / retnet) of a
     linear-attention or state-space model, else None."""
-    seen = {type(m).__name__ for m in model.modules()}
-    seen.add(type(model).__name__)
-    if "MambaMixer" in seen:
-        return "mamba"
-    if "Mamba2Mixer" in seen:
-        return "mamba2"
-    if "RwkvSelfAttention" in seen or "RwkvLinearAttention" in seen:
-        return "rwkv"
-    if "RecurrentGemmaRecurrentBlock" in seen:
-        return "recurrent_gemma"
-    if "RetNetAttention" in seen:
-        return "retnet"
+    for m in (model, *model.modules()):
+        fam = _NON_SOFTMAX_MIXERS.get(type(m).__name__)
+        if fam is not None:
+            return fam
     return None
 
 
@@ -212,8 +215,9 @@ def patch_model(model: torch.nn.Module) -> Tuple[str, int]:
     fam = _linear_attn_family(model)
     if fam is not None:
         raise RuntimeError(
-            f"flash-attn-volta only supports softmax MHA / GQA — model uses {fam}. "
-            "Refusing to patch a linear-attention / state-space architecture.")
+            f"cannot patch a {fam} model: this library replaces softmax attention "
+            "(multi-head or grouped-query) and the model mixes tokens with a "
+            "linear-attention / state-space layer instead")
     present = {type(m).__name__ for m in model.modules()}
     for fam_name, patch in (("gpt2", patch_gpt2), ("qwen3", patch_qwen3),
                             ("qwen2", patch_qwen2), ("llama", patch_llama)):

@@ -4,9 +4,14 @@
  * fp16 tensors are contiguous (batch, seqlen, nheads, head_dim) with 16-byte
  * aligned base addresses, LSE is contiguous (batch, nheads, seqlen) fp32.
  * `stream` is a cudaStream_t (NULL = legacy default stream).  `status` is an
- * optional device int the kernels OR error bits into (1 = a bounded on-device
- * wait ran out) instead of trapping; the host reads it when it wants to.
- * Calls are asynchronous, keep no state between calls and are thread-safe.
+ * optional device int the kernels OR error bits into instead of trapping; the
+ * host reads it when it wants to.  Bit 0 (1): a bounded on-device wait ran out.
+ * Bit 1 (2): a backward row term was beyond the range the kernel represents
+ * and was clamped (fp16: |LSE / sm_scale| or |rowsum(O * dO)| above ~1.3e8;
+ * bf16: above its largest finite value); the gradients of those rows are wrong.
+ * Calls are asynchronous and thread-safe.  All of them except
+ * fa_sm100_bwd_noalloc keep no state between calls; that one shares a static
+ * device array between calls (see its comment below).
  *
  * Return codes: FA_OK, or one of the FA_ERR_* values below
  * (fa_sm100_error_string() names them).
@@ -107,9 +112,12 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
  * fa_sm100_bwd_workspace_bytes() reports) lives in one static device array of
  * FA_SM100_NOALLOC_SCRATCH_BYTES (32 MiB) per GPU, held from library load
  * until process exit.  Shapes that need more return FA_ERR_SCRATCH_LIMIT
- * (e.g. head_dim 128 fits at most about 63k padded rows batch*nheads*seqlen).
+ * (e.g. head_dim 128 fits at most about 58k padded rows batch*nheads*seqlen:
+ * 576 bytes per row).
  * The first call on a device looks up the array's device address (with that
- * device current); make it before any stream capture.  All calls share the
+ * device current); make it before any stream capture.  The address is cached
+ * for the life of the process: a device or primary-context reset
+ * (cudaDeviceReset) after that first call is not supported.  All calls share the
  * array, so calls that overlap on the GPU race; inputs and outputs are still
  * caller-owned.  It calls no cudaMalloc / cudaFree.
  * No counterpart in the reference. */

@@ -62,10 +62,16 @@ def test_analytic_backward_equals_autograd(causal):
 
 
 def test_fully_masked_row_lse_is_inf():
-    # a (1,1,S,S) causal mask never masks a whole row; build one by hand
-    q, k, v = make_inputs(1, 8, 1, 16, seed=5, n=3)
-    o, lse = attention_fwd(q, k, v, causal=True)
-    assert torch.isfinite(lse).all()
+    # With a bottom-right causal mask and fewer keys than queries
+    # (causal_offset = Sk - Sq < 0) the first Sq - Sk query rows see no key:
+    # the reference's convention (triton_fa.py:152-159) is O = 0, LSE = +inf.
+    q, _, _ = make_inputs(1, 8, 2, 16, seed=5, n=3)
+    _, k, v = make_inputs(1, 5, 2, 16, seed=6, n=3)
+    o, lse = attention_fwd(q, k, v, causal=True, causal_offset=5 - 8, dtype=torch.float64)
+    assert torch.isposinf(lse[:, :, :3]).all()
+    assert torch.isfinite(lse[:, :, 3:]).all()
+    assert (o[:, :3] == 0).all()
+    # an empty sequence gives an empty LSE in the tiled recurrence
     _, lse_t = attention_fwd_tiled(q[:, :0], k[:, :0], v[:, :0])
     assert lse_t.numel() == 0
 

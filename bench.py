@@ -300,6 +300,7 @@ def run_ours(args, wl):
         hl_clocks.start()
         headline = bench_small("c3b", dev, args)
         headline["c3a"] = bench_small("c3a", dev, args)
+        headline["host_us_per_call"] = host_cost_us(dev)
         headline["clocks"] = hl_clocks.stop()
     mem_c3a = peak_mem_fwd_bwd(dev, 1, 4096, 16, 64, True)
     torch.cuda.empty_cache()
@@ -575,6 +576,28 @@ def peak_mem_fwd_bwd(dev, B, N, H, D, causal):
     peak = torch.cuda.max_memory_allocated(dev) - base
     del q, k, v, do
     return peak / 2**20
+
+
+def host_cost_us(dev, calls=2000):
+    """Host time per public-API call (microseconds): flash_attn_forward and
+    flash_attn_backward on a tiny shape (1, 128, 1, 64), whose kernels take a
+    few microseconds, so the host is the bottleneck of the loop."""
+    from flash_attn_volta_b200 import flash_attn_backward, flash_attn_forward
+    q, k, v, do = gen_shard(0, 1, 128, 1, 64, 1.0, dev, seed_base=5)
+    o, lse = flash_attn_forward(q, k, v, causal=True, return_softmax_lse=True)
+    res = {}
+    for name, fn in (("fwd", lambda: flash_attn_forward(q, k, v, causal=True)),
+                     ("bwd", lambda: flash_attn_backward(do, q, k, v, o, lse, causal=True))):
+        for _ in range(50):
+            fn()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            fn()
+        t1 = time.perf_counter()
+        torch.cuda.synchronize(dev)
+        res[name] = 1e6 * (t1 - t0) / calls
+    return res
 
 
 def bench_small(wl, dev, args):

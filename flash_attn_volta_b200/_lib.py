@@ -22,6 +22,7 @@ FA_ERR_WORKSPACE = 5
 FA_ERR_SCRATCH_LIMIT = 6
 
 STATUS_TIMEOUT = 1
+STATUS_RANGE = 2
 
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
@@ -89,25 +90,18 @@ def check(rc: int, what: str) -> None:
 
 
 # ----------------------------------------------------------------- status word
-_status: dict[int, torch.Tensor] = {}
-
-
 def status_word(device: torch.device) -> torch.Tensor:
-    """Per-device int32 the kernels OR error bits into (1 = on-device wait timed out)."""
+    """Per-device int32 the kernels OR error bits into (bit 0: an on-device wait
+    timed out; bit 1: a backward row term was clamped).  One word per device,
+    shared with the torch.ops.fav operators."""
+    from . import ops
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _status.get(idx)
-    if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-        _status[idx] = t
-    return t
+    return ops.status_word(idx)
 
 
 def status_ptr(idx: int) -> int:
     """Device address of the status word of CUDA device `idx`."""
-    t = _status.get(idx)
-    if t is None:
-        t = status_word(torch.device("cuda", idx))
-    return t.data_ptr()
+    return status_word(torch.device("cuda", idx)).data_ptr()
 
 
 def stream_ptr(idx: int) -> int:
@@ -144,14 +138,18 @@ class on_device:
 
 def check_status(device: torch.device | None = None) -> None:
     """Synchronise and raise RuntimeError if a kernel on `device` reported an error."""
-    devs = [device] if device is not None else [torch.device("cuda", i) for i in _status]
+    from . import ops
+    devs = ([device] if device is not None else
+            [torch.device("cuda", i) for i in ops.status_devices()])
     for d in devs:
         t = status_word(d)
         v = int(t.item())
         if v:
             t.zero_()
             raise RuntimeError(f"flash_attn_volta_b200 kernel reported status {v} on {d} "
-                               "(1 = an on-device wait timed out)")
+                               "(bit 0: an on-device wait timed out; bit 1: a backward row "
+                               "term, LSE/sm_scale or rowsum(O*dO), was beyond the range the "
+                               "kernel represents and was clamped)")
 
 
 _debug_sync = os.environ.get("FA_B200_SYNC_CHECK", "0") == "1"

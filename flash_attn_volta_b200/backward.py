@@ -3,8 +3,9 @@
 `flash_attn_backward(do, q, k, v, o, lse, causal, sm_scale) -> (dq, dk, dv)`
 keeps the reference's signature, AssertionError checks (triton_fa_bwd.py:609-614,
 :646) and default scale.  delta = rowsum(O*dO), the five backward GEMMs and
-the dQ conversion all run on the GPU behind fa_sm100_bwd; the fp32 workspace
-it needs comes from the torch caching allocator and is released on return.
+the dQ conversion all run on the GPU behind fa_sm100_bwd_ex, reached through
+the torch.ops.fav.bwd operator (csrc/torch_ops.cpp); the fp32 workspace it
+needs comes from the torch caching allocator and is released on return.
 """
 from __future__ import annotations
 
@@ -12,8 +13,8 @@ import math
 
 import torch
 
-from . import _lib
-from .forward import _as_kernel_input, _kv_heads
+from . import _lib, ops
+from .forward import _kv_heads
 
 
 def flash_attn_backward(
@@ -52,25 +53,9 @@ def flash_attn_backward(
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
 
-    do, q, k, v, o = (_as_kernel_input(t) for t in (do, q, k, v, o))
-    lse = lse.contiguous()
-    dq = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
-    dk = torch.empty((B, k.shape[1], Hkv, D), dtype=q.dtype, device=q.device)
-    dv = torch.empty_like(dk)
-    if q.numel() == 0 or k.shape[1] == 0:
-        return dq.zero_(), dk.zero_(), dv.zero_()
-    lib = _lib.load()
-    idx = q.device.index
-    with _lib.on_device(idx):
-        nbytes = lib.fa_sm100_bwd_workspace_bytes(B, N, H, D)
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-        rc = lib.fa_sm100_bwd_ex(do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                 o.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                 dv.data_ptr(), ws.data_ptr(), nbytes, B, N, k.shape[1], H, Hkv, D,
-                                 _lib.dtype_code(q.dtype), float(sm_scale), 1 if causal else 0,
-                                 _lib.status_ptr(idx), _lib.stream_ptr(idx))
-    if rc:
-        _lib.check(rc, "fa_sm100_bwd")
+    ops.load()
+    ops.note_device(q.device.index)
+    dq, dk, dv = torch.ops.fav.bwd(do, q, k, v, o, lse, bool(causal), float(sm_scale))
     if _lib.debug_sync():
         _lib.check_status(q.device)
     return dq, dk, dv

@@ -1,10 +1,13 @@
-"""Compile libfa_sm100.so in-tree for sm_100a with nvcc.
+"""Compile the package's native libraries in-tree.
 
-    python -m flash_attn_volta_b200.build [-v]
+    python -m flash_attn_volta_b200.build [-v] [-f]
 
-The library holds every CUDA kernel of the package plus the C ABI declared in
-include/fa_sm100.h.  It is built next to this file so that it travels with the
-source tree; nothing is installed into site-packages.
+libfa_sm100.so (nvcc, sm_100a) holds every CUDA kernel of the package plus the
+C ABI declared in include/fa_sm100.h.  libfa_torch_ops.so (g++ against
+PyTorch's headers) registers the torch.ops.fav operators on top of that C ABI
+and links libfa_sm100.so from its own directory.  Both are built next to this
+file so that they travel with the source tree; nothing is installed into
+site-packages.
 """
 from __future__ import annotations
 
@@ -24,8 +27,16 @@ NVCC_FLAGS = [
 ]
 
 
+OPS_NAME = "libfa_torch_ops.so"
+OPS_SOURCES = ["torch_ops.cpp"]
+
+
 def lib_path() -> str:
     return os.path.join(HERE, LIB_NAME)
+
+
+def ops_path() -> str:
+    return os.path.join(HERE, OPS_NAME)
 
 
 def _nvcc() -> str:
@@ -35,16 +46,56 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
 
 
-def _stale(out: str) -> bool:
+def _stale(out: str, deps: list[str] | None = None) -> bool:
     if not os.path.exists(out):
         return True
     t = os.path.getmtime(out)
-    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
-    deps.append(os.path.join(HERE, "..", "include", "fa_sm100.h"))
+    if deps is None:
+        deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f not in OPS_SOURCES]
+    deps = deps + [os.path.join(HERE, "..", "include", "fa_sm100.h")]
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Compile libfa_torch_ops.so (needs libfa_sm100.so built first)."""
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    out = ops_path()
+    deps = [os.path.join(CSRC, s) for s in OPS_SOURCES] + [lib_path()]
+    if not force and not _stale(out, deps):
+        return out
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    inc = ce.include_paths(device_type="cuda")
+    libdirs = ce.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = out + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", "-DTORCH_EXTENSION_NAME=fa_torch_ops"]
+    cmd += [f"-I{d}" for d in inc]
+    cmd += [os.path.join(CSRC, s) for s in OPS_SOURCES]
+    cmd += ["-o", tmp, f"-L{HERE}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN"]
+    cmd += [f"-L{d}" for d in libdirs]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda"]
+    if verbose:
+        print(" ".join(cmd))
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed with exit code {res.returncode}")
+    os.replace(tmp, out)
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Build libfa_sm100.so, then libfa_torch_ops.so; returns the former's path."""
+    out = _build_kernels(force, verbose)
+    build_torch_ops(force, verbose)
+    return out
+
+
+def _build_kernels(force: bool = False, verbose: bool = False) -> str:
     out = lib_path()
     if not force and not _stale(out):
         return out

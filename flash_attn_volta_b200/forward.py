@@ -3,7 +3,8 @@
 `flash_attn_forward` keeps the reference's signature, its AssertionError input
 checks (triton_fa.py:313-317), default scale (:319-320) and return convention
 (out, or (out, lse) with lse (B, H, N) fp32 natural log, +inf on fully masked
-rows).  The work runs in the sm_100a kernel behind fa_sm100_fwd; there is no
+rows).  The work runs in the sm_100a kernel behind fa_sm100_fwd_ex, reached
+through the torch.ops.fav.fwd operator (csrc/torch_ops.cpp); there is no
 padding of small head dims and no permute copy: the kernel reads the
 (B, N, H, D) tensors directly.
 """
@@ -13,16 +14,7 @@ import math
 
 import torch
 
-from . import _lib
-
-
-def _as_kernel_input(t: torch.Tensor) -> torch.Tensor:
-    """Contiguous (B, N, H, D) with a 16-byte aligned base (what TMA needs)."""
-    if not t.is_contiguous() or t.data_ptr() % 16 != 0:
-        t = t.contiguous()
-        if t.data_ptr() % 16 != 0:
-            t = t.clone()
-    return t
+from . import _lib, ops
 
 
 def _kv_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> int:
@@ -78,28 +70,11 @@ def flash_attn_forward(
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
 
-    q, k, v = _as_kernel_input(q), _as_kernel_input(k), _as_kernel_input(v)
-    out = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device)
-    lse = torch.empty((B, H, N), dtype=torch.float32, device=q.device) if return_softmax_lse else None
-    if q.numel() != 0 and k.shape[1] == 0:
-        # no keys at all: every query row is fully masked (O = 0, LSE = +inf)
-        out.zero_()
-        if lse is not None:
-            lse.fill_(float("inf"))
-    elif q.numel() != 0:
-        lib = _lib.load()
-        idx = q.device.index
-        with _lib.on_device(idx):
-            rc = lib.fa_sm100_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                                     lse.data_ptr() if lse is not None else None,
-                                     B, N, k.shape[1], H, Hkv, D, _lib.dtype_code(q.dtype),
-                                     float(sm_scale),
-                                     1 if causal else 0, _lib.status_ptr(idx),
-                                     _lib.stream_ptr(idx))
-        if rc:
-            _lib.check(rc, "fa_sm100_fwd_ex")
-        if _lib.debug_sync():
-            _lib.check_status(q.device)
+    ops.load()
+    ops.note_device(q.device.index)
+    out, lse = torch.ops.fav.fwd(q, k, v, bool(causal), float(sm_scale))
+    if _lib.debug_sync():
+        _lib.check_status(q.device)
     if return_softmax_lse:
         return out, lse
     return out

@@ -1,0 +1,91 @@
+"""torch.ops.fav: the PyTorch operators over the C ABI.
+
+Loads libfa_torch_ops.so (built in-tree next to this file, see build.py), which
+registers the CUDA kernels of ``fav::fwd`` and ``fav::bwd``, and registers here
+what torch needs besides: the shape functions used for FakeTensor / meta
+tracing (torch.compile, torch.export) and the autograd formula of ``fav::fwd``.
+
+There is no fallback: without the library every call raises RuntimeError.
+"""
+from __future__ import annotations
+
+import os
+import threading
+
+import torch
+
+from .build import ops_path
+
+_lock = threading.Lock()
+_loaded = False
+_status_devices: set[int] = set()  # devices whose status word exists
+
+
+def load() -> None:
+    """Load libfa_torch_ops.so once (raises RuntimeError when it is missing)."""
+    global _loaded
+    if _loaded:
+        return
+    with _lock:
+        if _loaded:
+            return
+        path = os.environ.get("FA_SM100_OPS_LIB") or ops_path()
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"{path} is missing: build it with `python -m flash_attn_volta_b200.build` "
+                "(the CUDA kernels have no fallback)")
+        torch.ops.load_library(path)
+        _register_python_parts()
+        _loaded = True
+
+
+def _register_python_parts() -> None:
+    @torch.library.register_fake("fav::fwd")
+    def _fwd_fake(q, k, v, causal, sm_scale):
+        B, S, H, _ = q.shape
+        return q.new_empty(q.shape), q.new_empty((B, H, S), dtype=torch.float32)
+
+    @torch.library.register_fake("fav::bwd")
+    def _bwd_fake(dout, q, k, v, out, lse, causal, sm_scale):
+        return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
+
+    def _setup(ctx, inputs, output):
+        q, k, v, causal, sm_scale = inputs
+        out, lse = output
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal = causal
+        ctx.sm_scale = sm_scale
+        ctx.mark_non_differentiable(lse)
+
+    def _backward(ctx, dout, dlse):
+        q, k, v, out, lse = ctx.saved_tensors
+        dout = dout.contiguous()
+        if dout.dtype != q.dtype:
+            dout = dout.to(q.dtype)
+        dq, dk, dv = torch.ops.fav.bwd(dout, q, k, v, out, lse, ctx.causal, ctx.sm_scale)
+        return dq, dk, dv, None, None
+
+    torch.library.register_autograd("fav::fwd", _backward, setup_context=_setup)
+
+
+def status_word(index: int) -> torch.Tensor:
+    """The int32 status word of CUDA device `index` that the operators pass to
+    the kernels (bit 0: an on-device wait timed out; bit 1: a row term was
+    clamped)."""
+    load()
+    _status_devices.add(index)
+    return torch.ops.fav.status(index)
+
+
+def note_device(index: int) -> None:
+    """Record that the operators ran on CUDA device `index` (they create its
+    status word), so that check_status() without a device looks there.  Not
+    recorded inside torch.compile tracing (a side effect dynamo refuses); the
+    word still exists and check_status(device) finds it."""
+    if not torch.compiler.is_compiling():
+        _status_devices.add(index)
+
+
+def status_devices() -> list[int]:
+    """CUDA devices whose status word has been created."""
+    return sorted(_status_devices)

@@ -159,3 +159,13 @@ def debug_sync() -> bool:
     """FA_B200_SYNC_CHECK=1 (read at import): synchronise and check the status
     word after every call."""
     return _debug_sync
+
+
+_deterministic = os.environ.get("FA_B200_DETERMINISTIC", "0") == "1"
+
+
+def deterministic_default() -> bool:
+    """Default dQ mode of the backward: FA_B200_DETERMINISTIC=1 (read at import)
+    selects the separate, bit-reproducible dQ kernel; otherwise dQ partials go
+    through L2 reductions."""
+    return _deterministic

@@ -16,7 +16,8 @@ from .forward import flash_attn_forward
 
 class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal: bool, sm_scale: float | None):
+    def forward(ctx, q, k, v, causal: bool, sm_scale: float | None,
+                deterministic: bool | None = None):
         if sm_scale is None:
             sm_scale = 1.0 / math.sqrt(q.shape[-1])
         out, lse = flash_attn_forward(q, k, v, causal=causal, sm_scale=sm_scale,
@@ -24,6 +25,7 @@ class _FlashAttnFn(torch.autograd.Function):
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal = causal
         ctx.sm_scale = sm_scale
+        ctx.deterministic = deterministic
         return out
 
     @staticmethod
@@ -32,13 +34,15 @@ class _FlashAttnFn(torch.autograd.Function):
         do = do.contiguous()
         if do.dtype != q.dtype:
             do = do.to(q.dtype)
-        dq, dk, dv = flash_attn_backward(do, q, k, v, out, lse,
-                                         causal=ctx.causal, sm_scale=ctx.sm_scale)
-        return dq, dk, dv, None, None
+        dq, dk, dv = flash_attn_backward(do, q, k, v, out, lse, causal=ctx.causal,
+                                         sm_scale=ctx.sm_scale,
+                                         deterministic=ctx.deterministic)
+        return dq, dk, dv, None, None, None
 
 
 def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-               causal: bool = False, sm_scale: float | None = None) -> torch.Tensor:
+               causal: bool = False, sm_scale: float | None = None, *,
+               deterministic: bool | None = None) -> torch.Tensor:
     """Attention with gradients: the B200 forward, and the B200 backward when
     autograd reaches it.
 
@@ -46,6 +50,7 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     head_dim one of 16, 32, 64, 128.  With ``causal`` each query attends only
     to keys at or before its own position.  ``sm_scale`` multiplies the scores
     before the softmax and defaults to head_dim ** -0.5.  The result has q's
-    shape and dtype.
+    shape and dtype.  ``deterministic`` selects the backward's dQ mode (see
+    flash_attn_backward).
     """
-    return _FlashAttnFn.apply(q, k, v, causal, sm_scale)
+    return _FlashAttnFn.apply(q, k, v, causal, sm_scale, deterministic)

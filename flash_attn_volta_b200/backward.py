@@ -26,6 +26,8 @@ def flash_attn_backward(
     lse: torch.Tensor,
     causal: bool = False,
     sm_scale: float | None = None,
+    *,
+    deterministic: bool | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """FlashAttention backward on B200 — fp16 (or bf16) in/out, fp32 accumulation.
 
@@ -35,6 +37,10 @@ def flash_attn_backward(
             H_kv heads, H % H_kv == 0, and N_k rows, as in the forward).
         lse: (B, H, N) fp32 log-sum-exp from the forward (+inf on fully masked rows).
         causal, sm_scale: must match the forward call.
+        deterministic: dQ from a separate kernel that sums each query row's key
+            blocks in a fixed order (bit-reproducible, like the reference's
+            atomics-free dQ kernel) instead of L2 reductions into an fp32
+            accumulator.  None = the package default (deterministic_default()).
 
     Returns:
         (dq, dk, dv), fp16, shaped like q, k and v (dk, dv sum over the query
@@ -55,7 +61,10 @@ def flash_attn_backward(
 
     ops.load()
     ops.note_device(q.device.index)
-    dq, dk, dv = torch.ops.fav.bwd(do, q, k, v, o, lse, bool(causal), float(sm_scale))
+    if deterministic is None:
+        deterministic = _lib.deterministic_default()
+    dq, dk, dv = torch.ops.fav.bwd(do, q, k, v, o, lse, bool(causal), float(sm_scale),
+                                   bool(deterministic))
     if _lib.debug_sync():
         _lib.check_status(q.device)
     return dq, dk, dv

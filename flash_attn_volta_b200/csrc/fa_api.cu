@@ -109,17 +109,21 @@ int make_bshd_map(CUtensorMap* m, const void* ptr, int B, int S, int H, int D, i
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WsLayout {
-  size_t dq_acc, q_aug, do_aug, total;
+  size_t dq_acc, q_aug, do_aug, delta, total;
 };
 
-WsLayout ws_layout(int B, int S, int H, int D) {
+// Backward workspace.  Fused dQ: fp32 dQ accumulator, then the extra-K-step
+// rows of Q and dO.  Separate dQ kernel (FA_BWD_DETERMINISTIC): the extra-K-step
+// rows and delta (fp32 per row); no accumulator.
+WsLayout ws_layout(int B, int S, int H, int D, bool sep) {
   const size_t S_pad = round_up((size_t)S, kSeqPad);
   const size_t rows = (size_t)B * H * S_pad;
   WsLayout w;
   w.dq_acc = 0;
-  w.q_aug = round_up(rows * D * sizeof(float), 256);
+  w.q_aug = sep ? 0 : round_up(rows * D * sizeof(float), 256);
   w.do_aug = w.q_aug + round_up(rows * kAugRowBytes, 256);
-  w.total = w.do_aug + round_up(rows * kAugRowBytes, 256);
+  w.delta = w.do_aug + round_up(rows * kAugRowBytes, 256);
+  w.total = w.delta + (sep ? round_up(rows * sizeof(float), 256) : 0);
   return w;
 }
 
@@ -213,7 +217,13 @@ int fa_sm100_fwd_ex(const void* q, const void* k, const void* v, void* out, floa
 
 size_t fa_sm100_bwd_workspace_bytes(int batch, int seqlen, int nheads, int head_dim) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return 0;
-  return ws_layout(batch, seqlen, nheads, head_dim).total;
+  return ws_layout(batch, seqlen, nheads, head_dim, false).total;
+}
+
+size_t fa_sm100_bwd_workspace_bytes_flags(int batch, int seqlen, int nheads, int head_dim,
+                                          int flags) {
+  if (!valid_shape(batch, seqlen, nheads, head_dim) || (flags & ~FA_BWD_DETERMINISTIC)) return 0;
+  return ws_layout(batch, seqlen, nheads, head_dim, (flags & FA_BWD_DETERMINISTIC) != 0).total;
 }
 
 }  // extern "C"
@@ -222,7 +232,7 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
                               const void* v, const void* out, const float* lse, void* dq, void* dk,
                               void* dv, void* workspace, size_t workspace_bytes, int batch, int seqlen,
                               int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
-                              float sm_scale, int causal, int* status, void* stream) {
+                              float sm_scale, int causal, int* status, void* stream, int flags) {
   if (!valid_shape(batch, seqlen, nheads, head_dim)) return FA_ERR_ARG;
   if (!valid_shape(batch, seqlen_k, nheads, head_dim)) return FA_ERR_ARG;
   if (nheads_kv < 1 || nheads % nheads_kv != 0) return FA_ERR_ARG;
@@ -231,7 +241,9 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   for (const void* p : ptrs)
     if (!p || !aligned16(p)) return FA_ERR_ARG;
   if (!lse || (reinterpret_cast<uintptr_t>(lse) & 3u)) return FA_ERR_ARG;
-  const WsLayout w = ws_layout(batch, seqlen, nheads, head_dim);
+  if (flags & ~FA_BWD_DETERMINISTIC) return FA_ERR_ARG;
+  const bool sep = (flags & FA_BWD_DETERMINISTIC) != 0;
+  const WsLayout w = ws_layout(batch, seqlen, nheads, head_dim, sep);
   if (!workspace || workspace_bytes < w.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return FA_ERR_WORKSPACE;
   int rc = check_device();
@@ -246,6 +258,13 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
     return rc;
   if ((rc = make_bshd_map(&tv, v, batch, seqlen_k, nheads_kv, head_dim, 128, dtype)) != FA_OK)
     return rc;
+  CUtensorMap tq128, tdo128;
+  if (sep) {
+    if ((rc = make_bshd_map(&tq128, q, batch, seqlen, nheads, head_dim, 128, dtype)) != FA_OK)
+      return rc;
+    if ((rc = make_bshd_map(&tdo128, dout, batch, seqlen, nheads, head_dim, 128, dtype)) != FA_OK)
+      return rc;
+  }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   BwdArgs a;
   a.tm_q = &tq;
@@ -258,7 +277,11 @@ int fa_sm100::bwd_impl(int phase, const void* dout, const void* q, const void* k
   a.dq = dq;
   a.dk = dk;
   a.dv = dv;
-  a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
+  a.dq_acc = sep ? nullptr : reinterpret_cast<float*>(ws + w.dq_acc);
+  a.dq_separate = sep ? 1 : 0;
+  a.tm_q128 = sep ? &tq128 : nullptr;
+  a.tm_do128 = sep ? &tdo128 : nullptr;
+  a.delta = sep ? reinterpret_cast<float*>(ws + w.delta) : nullptr;
   a.q_aug = ws + w.q_aug;
   a.do_aug = ws + w.do_aug;
   a.B = batch;
@@ -284,7 +307,7 @@ int fa_sm100_bwd(const void* dout, const void* q, const void* k, const void* v, 
                  float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
                   seqlen, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
-                  stream);
+                  stream, 0);
 }
 
 int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* v,
@@ -294,7 +317,17 @@ int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* 
                     float sm_scale, int causal, int* status, void* stream) {
   return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
                   seqlen_q, seqlen_k, nheads, nheads_kv, head_dim, dtype, sm_scale, causal, status,
-                  stream);
+                  stream, 0);
+}
+
+int fa_sm100_bwd_flags(const void* dout, const void* q, const void* k, const void* v,
+                       const void* out, const float* lse, void* dq, void* dk, void* dv,
+                       void* workspace, size_t workspace_bytes, int batch, int seqlen_q,
+                       int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+                       float sm_scale, int causal, int flags, int* status, void* stream) {
+  return bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
+                  seqlen_q, seqlen_k, nheads, nheads_kv, head_dim, dtype, sm_scale, causal, status,
+                  stream, flags);
 }
 
 int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k, const void* v,
@@ -304,7 +337,7 @@ int fa_sm100_bwd_phase(int phase, const void* dout, const void* q, const void* k
   if (phase < 0 || phase > 2) return FA_ERR_ARG;
   return bwd_impl(phase, dout, q, k, v, out, lse, dq, dk, dv, workspace, workspace_bytes, batch,
                   seqlen, seqlen, nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
-                  stream);
+                  stream, 0);
 }
 
 }  // extern "C"

@@ -189,14 +189,15 @@ __device__ __forceinline__ uint4 split_row(float x, int* status) {
 }
 
 // D/8 threads per (bh, row) of the padded row range, 16-byte loads of O and dO:
-// delta = rowsum(O * dO); the row's extra K-step entries [t0, t1, t2, 0, ...] of
-// -LSE/scale (Q side) and -delta (dO side); the row of the fp32 dQ accumulator
-// zeroed.
+// delta = rowsum(O * dO); the row's extra K-step entries [t0, t1, t2, a, 0, ...]
+// of -LSE/scale (Q side) and -delta (dO side); delta itself in fp32 when
+// `delta` is given (the separate dQ kernel reads it); the row of the fp32 dQ
+// accumulator zeroed when `dq_acc` is given (the fused dQ path).
 template <typename T>
 __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     const T* __restrict__ o, const T* __restrict__ dout, const float* __restrict__ lse,
     uint8_t* __restrict__ q_aug, uint8_t* __restrict__ do_aug, float* __restrict__ dq_acc,
-    int S /* query rows */,
+    float* __restrict__ delta, int S /* query rows */,
     int H, int D, int S_pad, float inv_scale, int* status) {
   griddep_wait();  // O and LSE come from the forward
   griddep_launch_dependents();
@@ -233,10 +234,13 @@ __global__ void __launch_bounds__(256) fa_bwd_pre_kernel(
     *reinterpret_cast<uint4*>(q_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 0)) = split_row<T>(-acc, status);
     *reinterpret_cast<uint4*>(do_aug + base + aug_offset(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
+    if (delta != nullptr) delta[prow] = acc;
   }
-  float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
-  qa[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-  qa[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (dq_acc != nullptr) {
+    float4* qa = reinterpret_cast<float4*>(dq_acc + prow * D) + sub * 2;
+    qa[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    qa[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
 // -------------------------------------------------------------------------- post
@@ -268,7 +272,10 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, T* __restri
 }
 
 // -------------------------------------------------------------------------- main
-template <int D, typename T>
+// DQ: also compute dQ (partial per key tile, added into the fp32 accumulator
+// with bulk L2 reductions); without it the kernel computes dK and dV only and
+// dQ comes from fa_bwd_dq_kernel.
+template <int D, typename T, bool DQ>
 __global__ void __launch_bounds__(544, 1)
     fa_bwd_main_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
@@ -346,9 +353,11 @@ __global__ void __launch_bounds__(544, 1)
     for (int i = 0; i < C_COUNT; ++i) {
       uint32_t cnt = 1;
       if (i == C_SFREE || i == C_DSREADY) cnt = 8;
-      if (i == C_SFULL || i == C_PFREE) cnt = 2;  // two issuing threads commit
-      if (i == C_DQFREE || i == C_DRAIN) cnt = 4;
-      if (i == C_KVEMPTY) cnt = 3;
+      if (i == C_SFULL) cnt = 2;  // two issuing threads commit
+      if (i == C_PFREE) cnt = DQ ? 2 : 1;
+      if (i == C_DQFREE) cnt = 4;
+      if (i == C_DRAIN) cnt = DQ ? 4 : 3;
+      if (i == C_KVEMPTY) cnt = DQ ? 3 : 2;
       if (i == C_DKVFREE) cnt = 8;
       mbar_init(bar(i), cnt);
     }
@@ -475,7 +484,7 @@ __global__ void __launch_bounds__(544, 1)
     // chains expect one arrival per chain (SFULL: 0+1, PFREE: 2+3).  Tile i's
     // S^T / dP^T are complete before the softmax warps signal DSREADY(i).
     const int role = warp - 13;
-    if (lane == 0) {
+    if (lane == 0 && (DQ || role != 3)) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
       constexpr uint32_t ab = Elem<T>::kIdescAB;
       constexpr uint32_t id_s = make_idesc_f16(C::BN, C::BM, false, false) | ab;  // S^T, dP^T
@@ -549,7 +558,7 @@ __global__ void __launch_bounds__(544, 1)
             mma_commit(bar(C_QEMPTY + st));
             mma_commit(bar(C_PFREE));
             TRACE(6, gi);
-          } else {
+          } else if constexpr (DQ) {
             if (!mbar_wait(bar(C_DSREADY), (uint32_t)gi & 1u, wc) ||
                 (gi > 0 && !mbar_wait(bar(C_DQFREE), (uint32_t)(gi - 1) & 1u, wc))) {
               ok = false;
@@ -685,13 +694,15 @@ __global__ void __launch_bounds__(544, 1)
           // col] K-major SW128 shared tile (64-column atoms) that the dQ MMA reads.
           tmem_st16(tmem + lane_base + C::COL_PT + cb / 2, pp);
           if constexpr (C::DS_TMEM) tmem_st16(tmem + lane_base + C::COL_DST + cb / 2, dd);
-          const int a = cb / 64;
-          const int ch0 = (cb % 64) / 8;
-          const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
+          if constexpr (DQ || !C::DS_TMEM) {
+            const int a = cb / 64;
+            const int ch0 = (cb % 64) / 8;
+            const uint32_t sb = sbase + C::OFF_DS + a * C::BN * 128;
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
-                         dd[4 * u + 3]);
+            for (int u = 0; u < 4; ++u)
+              st_shared_v4(sb + sw128_offset(r, ch0 + u), dd[4 * u], dd[4 * u + 1], dd[4 * u + 2],
+                           dd[4 * u + 3]);
+          }
         }
         if (!ok) break;
         tmem_wait_st();
@@ -739,7 +750,7 @@ __global__ void __launch_bounds__(544, 1)
       gs += nit;
       ++nt;
     }
-  } else if (warp < 12) {
+  } else if (DQ && warp < 12) {
     // ------------------------------------------------------------ dQ epilogue warps 8..11
     // Each tile's dQ partial goes TMEM -> registers -> shared memory ([q][d] fp32,
     // the accumulator's own layout) -> one bulk fp32 reduction into global memory.
@@ -837,11 +848,11 @@ __global__ void __launch_bounds__(544, 1)
   }
 }
 
-template <int D, typename T>
+template <int D, typename T, bool DQ>
 static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   using C = BwdCfg<D>;
-  constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000);
-  if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T>), C::SMEM))
+  constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000) + (DQ ? 0 : 4000);
+  if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T, DQ>), C::SMEM))
     return FA_ERR_LAUNCH;
   const int ntiles = a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN);
   const int nsm = sm_count();
@@ -849,7 +860,7 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   const int g = tile_grid(ntiles, nsm);
   dim3 grid(g);
   const cudaError_t e = launch_pdl(
-      fa_bwd_main_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
+      fa_bwd_main_kernel<D, T, DQ>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,
       *a.tm_k, *a.tm_v, a.q_aug, a.do_aug, a.dq_acc, static_cast<T*>(a.dk), static_cast<T*>(a.dv),
       a.Sq, a.Sk, a.H, a.H / a.Hkv, a.S_pad, ntiles, tile_window(ntiles, g), a.scale,
       a.scale * 1.4426950408889634f,
@@ -863,24 +874,29 @@ int bwd_q_rows(int D) { return D == 128 ? 64 : 128; }
 
 template <typename T>
 static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream, int phase) {
+  const bool sep = a.dq_separate != 0;
   if (phase < 0 || phase == 0) {
     const int rows_per_block = 256 / (a.D / 8);
     dim3 grid((a.S_pad + rows_per_block - 1) / rows_per_block, a.B * a.H);
     if (launch_pdl(fa_bwd_pre_kernel<T>, grid, dim3(256), 0, stream, static_cast<const T*>(a.o),
-                   static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug, a.dq_acc, a.Sq, a.H,
-                   a.D, a.S_pad, 1.0f / a.scale, a.status) != cudaSuccess)
+                   static_cast<const T*>(a.dout), a.lse, a.q_aug, a.do_aug,
+                   sep ? nullptr : a.dq_acc, sep ? a.delta : nullptr, a.Sq, a.H, a.D, a.S_pad,
+                   1.0f / a.scale, a.status) != cudaSuccess)
       return FA_ERR_LAUNCH;
   }
   int rc = FA_OK;
-  if (phase < 0 || phase == 1) switch (a.D) {
-    case 16: rc = launch_bwd_main<16, T>(a, stream); break;
-    case 32: rc = launch_bwd_main<32, T>(a, stream); break;
-    case 64: rc = launch_bwd_main<64, T>(a, stream); break;
-    case 128: rc = launch_bwd_main<128, T>(a, stream); break;
-    default: return FA_ERR_ARG;
+  if (phase < 0 || phase == 1) {
+    switch (a.D) {
+      case 16: rc = sep ? launch_bwd_main<16, T, false>(a, stream) : launch_bwd_main<16, T, true>(a, stream); break;
+      case 32: rc = sep ? launch_bwd_main<32, T, false>(a, stream) : launch_bwd_main<32, T, true>(a, stream); break;
+      case 64: rc = sep ? launch_bwd_main<64, T, false>(a, stream) : launch_bwd_main<64, T, true>(a, stream); break;
+      case 128: rc = sep ? launch_bwd_main<128, T, false>(a, stream) : launch_bwd_main<128, T, true>(a, stream); break;
+      default: return FA_ERR_ARG;
+    }
   }
   if (rc != FA_OK) return rc;
   if (phase < 0 || phase == 2) {
+    if (sep) return launch_bwd_dq(a, stream);
     const int per_row = a.D / 8;
     const size_t n = (size_t)a.Sq * per_row;
     dim3 grid((unsigned)((n + 255) / 256), a.B * a.H);

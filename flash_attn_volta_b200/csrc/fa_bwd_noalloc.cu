@@ -62,5 +62,5 @@ extern "C" int fa_sm100_bwd_noalloc(const void* dout, const void* q, const void*
   return fa_sm100::bwd_impl(-1, dout, q, k, v, out, lse, dq, dk, dv, scratch,
                             (size_t)FA_SM100_NOALLOC_SCRATCH_BYTES, batch, seqlen, seqlen,
                             nheads, nheads, head_dim, FA_DTYPE_F16, sm_scale, causal, status,
-                            stream);
+                            stream, 0);
 }

@@ -54,6 +54,14 @@ struct BwdArgs {
   int causal;
   int* status;
   unsigned long long timeout_ns;
+  // dQ mode.  0: fused into the main kernel (partials added into dq_acc with L2
+  // reductions, then converted by fa_bwd_post).  1: the main kernel computes
+  // dK / dV only and fa_bwd_dq_kernel computes dQ per query tile in a fixed
+  // key order (deterministic; needs tm_q128 / tm_do128 and delta).
+  int dq_separate = 0;
+  const CUtensorMap* tm_q128 = nullptr;   // box rows: 128
+  const CUtensorMap* tm_do128 = nullptr;  // box rows: 128
+  float* delta = nullptr;  // (B*H, S_pad) fp32 rowsum(O * dO), written by fa_bwd_pre
 };
 
 namespace {
@@ -132,6 +140,8 @@ constexpr int kAugBig = 2048;
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 // phase -1: all three kernels; 0: delta/LSE prep; 1: main kernel; 2: dQ conversion
 int launch_bwd(const BwdArgs& a, cudaStream_t stream, int phase);
+// the separate dQ kernel (BwdArgs::dq_separate); fa_bwd_dq.cu
+int launch_bwd_dq(const BwdArgs& a, cudaStream_t stream);
 int bwd_q_rows(int D);
 
 // Argument checks, tensor maps and launches of the backward on a caller-given
@@ -140,7 +150,7 @@ int bwd_impl(int phase, const void* dout, const void* q, const void* k, const vo
              const void* out, const float* lse, void* dq, void* dk, void* dv, void* workspace,
              size_t workspace_bytes, int batch, int seqlen, int seqlen_k, int nheads,
              int nheads_kv, int head_dim, int dtype, float sm_scale, int causal, int* status,
-             void* stream);
+             void* stream, int flags);
 
 // sequence rows are padded to a multiple of this in the backward workspace
 constexpr int kSeqPad = 128;

@@ -1,7 +1,8 @@
 // PyTorch operators over the C ABI of libfa_sm100.so (include/fa_sm100.h).
 //
 //   torch.ops.fav.fwd(q, k, v, causal, sm_scale) -> (out, lse)
-//   torch.ops.fav.bwd(dout, q, k, v, out, lse, causal, sm_scale) -> (dq, dk, dv)
+//   torch.ops.fav.bwd(dout, q, k, v, out, lse, causal, sm_scale, deterministic=False)
+//       -> (dq, dk, dv)
 //   torch.ops.fav.status(device) -> the device's int32 status word
 //
 // These are the only callers of the C core on the Python side
@@ -100,7 +101,7 @@ std::tuple<at::Tensor, at::Tensor> fwd_cuda(const at::Tensor& q_in, const at::Te
 std::tuple<at::Tensor, at::Tensor, at::Tensor> bwd_cuda(
     const at::Tensor& dout_in, const at::Tensor& q_in, const at::Tensor& k_in,
     const at::Tensor& v_in, const at::Tensor& out_in, const at::Tensor& lse_in, bool causal,
-    double sm_scale) {
+    double sm_scale, bool deterministic) {
   const at::Tensor dout = kernel_input(dout_in, "dout");
   const at::Tensor q = kernel_input(q_in, "q");
   const at::Tensor k = kernel_input(k_in, "k");
@@ -121,16 +122,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> bwd_cuda(
     dv.zero_();
     return {dq, dk, dv};
   }
-  const size_t nbytes = fa_sm100_bwd_workspace_bytes((int)B, (int)Sq, (int)H, (int)D);
+  const int flags = deterministic ? FA_BWD_DETERMINISTIC : 0;
+  const size_t nbytes = fa_sm100_bwd_workspace_bytes_flags((int)B, (int)Sq, (int)H, (int)D, flags);
   TORCH_CHECK(nbytes > 0, "fa_sm100_bwd_workspace_bytes: unsupported shape");
   at::Tensor ws = at::empty({(int64_t)nbytes}, q.options().dtype(at::kByte));
   at::Tensor st = status_word(q.get_device());
-  const int rc = fa_sm100_bwd_ex(
+  const int rc = fa_sm100_bwd_flags(
       dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
       lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), nbytes,
       (int)B, (int)Sq, (int)Sk, (int)H, (int)Hkv, (int)D, dt, (float)sm_scale, causal ? 1 : 0,
-      st.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
-  check_rc(rc, "fa_sm100_bwd_ex");
+      flags, st.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc, "fa_sm100_bwd_flags");
   return {dq, dk, dv};
 }
 
@@ -140,7 +142,7 @@ TORCH_LIBRARY(fav, m) {
   m.def("fwd(Tensor q, Tensor k, Tensor v, bool causal, float sm_scale) -> (Tensor, Tensor)");
   m.def(
       "bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor out, Tensor lse, bool causal, "
-      "float sm_scale) -> (Tensor, Tensor, Tensor)");
+      "float sm_scale, bool deterministic=False) -> (Tensor, Tensor, Tensor)");
   m.def("status(int device) -> Tensor", &status_word);
 }
 

@@ -46,7 +46,7 @@ def _register_python_parts() -> None:
         return q.new_empty(q.shape), q.new_empty((B, H, S), dtype=torch.float32)
 
     @torch.library.register_fake("fav::bwd")
-    def _bwd_fake(dout, q, k, v, out, lse, causal, sm_scale):
+    def _bwd_fake(dout, q, k, v, out, lse, causal, sm_scale, deterministic=False):
         return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
 
     def _setup(ctx, inputs, output):
@@ -62,7 +62,9 @@ def _register_python_parts() -> None:
         dout = dout.contiguous()
         if dout.dtype != q.dtype:
             dout = dout.to(q.dtype)
-        dq, dk, dv = torch.ops.fav.bwd(dout, q, k, v, out, lse, ctx.causal, ctx.sm_scale)
+        from ._lib import deterministic_default
+        dq, dk, dv = torch.ops.fav.bwd(dout, q, k, v, out, lse, ctx.causal, ctx.sm_scale,
+                                       deterministic_default())
         return dq, dk, dv, None, None
 
     torch.library.register_autograd("fav::fwd", _backward, setup_context=_setup)

@@ -37,7 +37,7 @@ extern "C" {
 /* Size of the static device scratch array behind fa_sm100_bwd_noalloc. */
 #define FA_SM100_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
-#define FA_SM100_ABI_VERSION 2
+#define FA_SM100_ABI_VERSION 3
 
 /* Element types of the _ex entry points (q, k, v, out, dout, dq, dk, dv). */
 #define FA_DTYPE_F16 0
@@ -91,6 +91,27 @@ int fa_sm100_bwd_ex(const void* dout, const void* q, const void* k, const void* 
                     void* workspace, size_t workspace_bytes, int batch, int seqlen_q,
                     int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
                     float sm_scale, int causal, int* status, void* stream);
+
+/* Flags of fa_sm100_bwd_flags.
+ * FA_BWD_DETERMINISTIC: dQ from its own kernel, one CTA per 128-row query tile
+ * summing its key blocks in ascending order inside tensor memory (no atomics),
+ * as the reference's dQ kernel does (flash_attn_volta/triton_fa_bwd.py:73-307);
+ * the main kernel then computes dK and dV only.  dQ is bit-reproducible from
+ * run to run and the workspace holds no fp32 dQ accumulator.  Without the flag
+ * dQ partials are added into an fp32 accumulator with L2 reductions whose
+ * order varies between runs. */
+#define FA_BWD_DETERMINISTIC 1
+
+/* Backward with flags (FA_BWD_*); otherwise as fa_sm100_bwd_ex.  The workspace
+ * is fa_sm100_bwd_workspace_bytes_flags() bytes (fa_sm100_bwd_workspace_bytes()
+ * is always enough).  Same computation as flash_attn_volta/triton_fa_bwd.py:587-700. */
+int fa_sm100_bwd_flags(const void* dout, const void* q, const void* k, const void* v,
+                       const void* out, const float* lse, void* dq, void* dk, void* dv,
+                       void* workspace, size_t workspace_bytes, int batch, int seqlen_q,
+                       int seqlen_k, int nheads, int nheads_kv, int head_dim, int dtype,
+                       float sm_scale, int causal, int flags, int* status, void* stream);
+size_t fa_sm100_bwd_workspace_bytes_flags(int batch, int seqlen, int nheads, int head_dim,
+                                          int flags);
 
 /* The three launches fa_sm100_bwd makes, one at a time, on the same arguments:
  * phase 0 = delta and the -LSE/scale, -delta MMA terms, zeroing of the dQ accumulator,

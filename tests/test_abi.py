@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert "fa_sm100_fwd" in names and "fa_sm100_bwd" in names
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/ but not exported"
-    assert lib.fa_sm100_abi_version() == 2
+    assert lib.fa_sm100_abi_version() == 3
 
 
 def test_error_strings():

@@ -381,6 +381,21 @@ def run_ours(args, wl):
             dist.destroy_process_group()
         return
 
+    # ---------------- the same step with the deterministic backward (dQ kernel)
+    def step_det():
+        q.grad = k.grad = v.grad = None
+        flash_attn(q, k, v, causal=causal, deterministic=True).backward(do)
+
+    for _ in range(2):
+        step_det()
+    det_steps = max(3, min(args.steps, 10))
+    det_ms = time_steps(step_det, det_steps, stream) / det_steps
+    if world > 1:
+        t = torch.tensor([det_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        det_ms = float(t.item())
+    q.grad = k.grad = v.grad = None
+
     # ---------------- e2e: pinned host -> device, step, results -> pinned host
     # Every step copies its inputs (q, k, v, dO) in from pinned host memory and
     # its results (O, dQ, dK, dV) back out, inside the timed region.  Three
@@ -531,6 +546,10 @@ def run_ours(args, wl):
                             "peak_tflops": world * peak_sus,
                             "kind": f"{peak_kind} bf16 sustained x n_gpus"},
             "gpu_launches": 4 * args.steps,
+            "deterministic": {"ms_per_step": det_ms,
+                              "tflops": 2.5 * flops_fwd(B, S, H, D, causal) / (det_ms * 1e-3) / 1e12,
+                              "what": "same step with deterministic=True (dQ from the "
+                                      "query-tile kernel, bit-reproducible)"},
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nb,
                     "d2h_bytes_per_step": 4 * nb, "steps": e2e_steps,
                     "overlap": "copy-in of step i+1 and copy-out of step i-1 run beside "
@@ -614,6 +633,10 @@ def bench_small(wl, dev, args):
         q.grad = k.grad = v.grad = None
         flash_attn(q, k, v, causal=causal).backward(do)
 
+    def fwd_bwd_det():
+        q.grad = k.grad = v.grad = None
+        flash_attn(q, k, v, causal=causal, deterministic=True).backward(do)
+
     def fwd_lse():
         with torch.no_grad():
             flash_attn_forward(q, k, v, causal=causal, return_softmax_lse=True)
@@ -631,12 +654,14 @@ def bench_small(wl, dev, args):
                 ts.append(e0.elapsed_time(e1))
         return statistics.median(ts)
 
-    ms, fms = median_ms(fwd_bwd), median_ms(fwd_lse)
+    ms, fms, dms = median_ms(fwd_bwd), median_ms(fwd_lse), median_ms(fwd_bwd_det)
     ff = flops_fwd(B, S, H, D, causal)
     return {"B": B, "S": S, "H": H, "D": D, "causal": causal, "ms_per_step": ms,
             "tflops": 2.5 * ff / (ms * 1e-3) / 1e12,
             "tflops_alg": 3.5 * ff / (ms * 1e-3) / 1e12,
             "fwd_lse_ms": fms, "fwd_lse_tflops": ff / (fms * 1e-3) / 1e12,
+            "deterministic_ms_per_step": dms,
+            "deterministic_tflops": 2.5 * ff / (dms * 1e-3) / 1e12,
             "flop_convention": "tflops: 2.5 x F_fwd; tflops_alg: 3.5 x F_fwd (2 forward + "
                                "5 backward GEMMs); fwd_lse: F_fwd",
             "l2": "flushed (256 MiB write) before each step"}

@@ -100,7 +100,8 @@ def _build_kernels(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale(out):
         return out
     tmp = out + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
+    extra = os.environ.get("FA_SM100_NVCC_EXTRA", "").split()
+    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))

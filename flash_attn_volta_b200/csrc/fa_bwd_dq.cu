@@ -10,10 +10,10 @@
 // fixed order, so dQ is bit-reproducible.  The main backward kernel
 // (fa_bwd_main_kernel<D, T, false>) computes dK and dV next to it.
 //
-// A CTA walks a list of query tiles (longest first under a causal mask,
-// persistent for at most 4 tiles per SM, like the forward).  Tensor memory
+// One persistent CTA per SM walks a list of query tiles (longest first under a
+// causal mask, snake order over the rounds, like the forward).  Tensor memory
 // (512 columns): S [0,128) and dP [128,256) (fp32, one buffer each: the
-// dS warps copy them to registers and release them at once, so the next
+// dS warps copy all of their columns to registers and release them at once, so the next
 // key block's S and dP MMAs run during the math), dS [256,384) as element-type
 // pairs in two buffers of 64 columns (the A operand of dQ += dS K), dQ
 // [384, 384+D).  Warp roles:
@@ -337,29 +337,33 @@ __global__ void __launch_bounds__(352, 1)
         const int kv0 = j * C::BN;
         // every (query, key) pair of this block is unmasked
         const bool full = (kv0 + C::BN <= Sk) && (!causal || kv0 + C::BN - 1 <= tl.q0 + off);
+        // all 64 columns of S and dP into registers, then release them at once
+        // (the next key block's S and dP MMAs run during the math below)
+        uint32_t sr[2][32], dr[2][32];
+        tmem_ld32(tmem + lane_base + C::COL_S + c0, sr[0]);
+        tmem_ld32(tmem + lane_base + C::COL_DP + c0, dr[0]);
+        tmem_ld32(tmem + lane_base + C::COL_S + c0 + 32, sr[1]);
+        tmem_ld32(tmem + lane_base + C::COL_DP + c0 + 32, dr[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(S_FREE));
+#pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int cb = c0 + cc * 32;  // first key column of this chunk
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + C::COL_S + cb, sr);
-          tmem_ld32(tmem + lane_base + C::COL_DP + cb, dr);
-          tmem_wait_ld();
-          if (cc == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(S_FREE));
-          }
           uint32_t dd[16];
           if (full) {
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
               float x0, x1;
-              f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])),
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[cc][2 * k]),
+                                       __uint_as_float(sr[cc][2 * k + 1])),
                                c2, nl2),
                         x0, x1);
               const uint64_t p2 = f2_pack(ex2(x0), ex2(x1));
               float d0, d1;
-              f2_unpack(f2_mul(p2, f2_add(f2_pack(__uint_as_float(dr[2 * k]),
-                                                  __uint_as_float(dr[2 * k + 1])),
+              f2_unpack(f2_mul(p2, f2_add(f2_pack(__uint_as_float(dr[cc][2 * k]),
+                                                  __uint_as_float(dr[cc][2 * k + 1])),
                                           ndl)),
                         d0, d1);
               dd[k] = Elem<T>::pack2(d0, d1);
@@ -372,9 +376,9 @@ __global__ void __launch_bounds__(352, 1)
               for (int u = 0; u < 2; ++u) {
                 const int kv = kv0 + cb + 2 * k + u;
                 const bool valid = kv < Sk && (!causal || kv <= q_idx + off);
-                const float p = valid ? ex2(fmaf(__uint_as_float(sr[2 * k + u]), scale_log2, -l2))
-                                      : 0.f;
-                d2[u] = p * (__uint_as_float(dr[2 * k + u]) - dl);
+                const float p =
+                    valid ? ex2(fmaf(__uint_as_float(sr[cc][2 * k + u]), scale_log2, -l2)) : 0.f;
+                d2[u] = p * (__uint_as_float(dr[cc][2 * k + u]) - dl);
               }
               dd[k] = Elem<T>::pack2(d2[0], d2[1]);
             }
@@ -446,7 +450,10 @@ static int launch_dq_d(const BwdArgs& a, cudaStream_t stream) {
   const int ntiles = a.B * a.H * ((a.Sq + C::BM - 1) / C::BM);
   const int nsm = sm_count();
   if (nsm <= 0) return FA_ERR_DEVICE;
-  const int g = tile_grid(ntiles, nsm);
+  // always persistent (one CTA per SM walking the tile list): measured at
+  // B=1, S=8192, H=16, D=128 the grid of one CTA per tile was 7 % slower (the
+  // next tile's Q / dO load and first MMAs overlap this tile's last step here)
+  const int g = ntiles < nsm ? ntiles : nsm;
   const cudaError_t e = launch_pdl(
       fa_bwd_dq_kernel<D, T>, dim3(g), dim3(C::THREADS), C::SMEM, stream, *a.tm_q128,
       *a.tm_do128, *a.tm_k, *a.tm_v, a.lse, static_cast<const float*>(a.delta),

@@ -14,13 +14,15 @@ kernels:
   causal mask every block is full).  Every block is a square C x C attention —
   exactly what the single-GPU kernel computes — returning (O_ij, LSE_ij); the
   partial results are merged with lse = logaddexp(lse, lse_ij) and
-  O = sum_j exp(lse_ij - lse) O_ij in fp32.  The next K/V block is exchanged
-  (batch_isend_irecv to r+1 / from r-1) while the current one is computed.
+  O = sum_j exp(lse_ij - lse) O_ij in fp32 (each O_ij arrives rounded to the
+  element type by the kernel).  The next K and V blocks are exchanged (one
+  batched isend/irecv to r+1 / from r-1) while the current one is computed.
 * Backward: the same ring; each block's (dq, dk, dv) come from the single-GPU
   backward fed with the *final* O and LSE (so P and delta are the global ones,
   as in the reference's Algorithm-4 backward); dq accumulates locally and
-  dk/dv accumulate in an fp32 buffer that travels with its K/V block and makes
-  one last hop back to its owner.
+  dk/dv accumulate in fp32 buffers that travel with their K/V block and make
+  one last hop back to their owner.  A step's contribution is computed into a
+  fresh buffer while the accumulator arrives, so that hop overlaps compute too.
 
 Received blocks land in local buffers before a kernel reads them: no kernel
 touches another GPU's memory.
@@ -93,14 +95,26 @@ def _merge(acc_o, acc_lse, o, lse):
     return acc_o * w_old + o * w_new, new
 
 
-def _exchange(send: torch.Tensor, group, rank: int, world: int):
-    """Start sending `send` to rank+1 and receiving the same shape from rank-1."""
-    recv = torch.empty_like(send)
+def _peers(group, rank: int, world: int):
     nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
     prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
-    ops = [dist.P2POp(dist.isend, send, nxt, group), dist.P2POp(dist.irecv, recv, prv, group)]
-    reqs = dist.batch_isend_irecv(ops)
-    return recv, reqs
+    return nxt, prv
+
+
+def _exchange(sends, group, rank: int, world: int):
+    """Start sending each tensor of `sends` to rank+1 and receiving tensors of
+    the same shapes from rank-1 (one batched NCCL call); returns (recvs, works)."""
+    nxt, prv = _peers(group, rank, world)
+    recvs = [torch.empty_like(t) for t in sends]
+    ops = [dist.P2POp(dist.isend, t, nxt, group) for t in sends]
+    ops += [dist.P2POp(dist.irecv, t, prv, group) for t in recvs]
+    return recvs, dist.batch_isend_irecv(ops)
+
+
+def _finish(works):
+    # NCCL works: the current stream waits on the device; the host does not block
+    for w in works:
+        w.wait()
 
 
 def _world(group):
@@ -111,13 +125,14 @@ def _world(group):
 
 def _ring_forward(q2, k2, v2, causal, scale, group):
     rank, world = _world(group)
-    q = q2.chunk(2, dim=1)
+    q = [c.contiguous() for c in q2.chunk(2, dim=1)]
     ids_q = zigzag_chunk_ids(rank, world)
-    kv = torch.stack([k2, v2])  # (2, B, 2C, H, D): travels as one buffer
+    kv = (k2, v2)
     acc = [[None, None], [None, None]]  # per query chunk: [o, lse]
     for step in range(world):
         src = (rank - step) % world
         ids_k = zigzag_chunk_ids(src, world)
+        # the next K/V block travels while this one is computed
         pending = _exchange(kv, group, rank, world) if step < world - 1 else None
         ks, vs = kv[0].chunk(2, dim=1), kv[1].chunk(2, dim=1)
         for a in range(2):
@@ -125,14 +140,12 @@ def _ring_forward(q2, k2, v2, causal, scale, group):
                 mode = _block_mode(ids_q[a], ids_k[b], causal)
                 if mode is None:
                     continue
-                o, lse = block_fwd(q[a].contiguous(), ks[b].contiguous(), vs[b].contiguous(),
-                                   mode, scale)
+                o, lse = block_fwd(q[a], ks[b].contiguous(), vs[b].contiguous(), mode, scale)
                 acc[a] = list(_merge(acc[a][0], acc[a][1], o, lse))
         if pending is not None:
-            recv, reqs = pending
-            for r in reqs:
-                r.wait()
-            kv = recv
+            recvs, works = pending
+            _finish(works)
+            kv = tuple(recvs)
     o = torch.cat([acc[0][0], acc[1][0]], dim=1).to(q2.dtype)
     lse = torch.cat([acc[0][1], acc[1][1]], dim=2).contiguous()
     return o, lse
@@ -140,43 +153,53 @@ def _ring_forward(q2, k2, v2, causal, scale, group):
 
 def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
     rank, world = _world(group)
-    q, do, o = q2.chunk(2, dim=1), do2.chunk(2, dim=1), o2.chunk(2, dim=1)
-    lse = lse2.chunk(2, dim=2)
+    q = [c.contiguous() for c in q2.chunk(2, dim=1)]
+    do = [c.contiguous() for c in do2.chunk(2, dim=1)]
+    o = [c.contiguous() for c in o2.chunk(2, dim=1)]
+    lse = [c.contiguous() for c in lse2.chunk(2, dim=2)]
     ids_q = zigzag_chunk_ids(rank, world)
     dq = torch.zeros(q2.shape, dtype=torch.float32, device=q2.device)
     dqs = dq.chunk(2, dim=1)
-    kv = torch.stack([k2, v2])
-    dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q2.device)
+    kv = (k2, v2)
+    # dK / dV of the K/V block a rank holds travel with it, in fp32.  At step s
+    # the accumulator of block (rank - s) arrives from rank-1 while this rank
+    # computes that block's contribution into a fresh buffer; the two are added
+    # once both are there and sent on, so the hop overlaps the next step.
+    dkv_in = None  # (recvs, works) of the accumulator arriving for this step's block
     for step in range(world):
         src = (rank - step) % world
         ids_k = zigzag_chunk_ids(src, world)
         pending = _exchange(kv, group, rank, world) if step < world - 1 else None
         ks, vs = kv[0].chunk(2, dim=1), kv[1].chunk(2, dim=1)
-        dks, dvs = dkv[0].chunk(2, dim=1), dkv[1].chunk(2, dim=1)
+        part_k = torch.zeros(k2.shape, dtype=torch.float32, device=q2.device)
+        part_v = torch.zeros(v2.shape, dtype=torch.float32, device=q2.device)
+        pks, pvs = part_k.chunk(2, dim=1), part_v.chunk(2, dim=1)
         for a in range(2):
             for b in range(2):
                 mode = _block_mode(ids_q[a], ids_k[b], causal)
                 if mode is None:
                     continue
-                g = block_bwd(do[a].contiguous(), q[a].contiguous(), ks[b].contiguous(),
-                              vs[b].contiguous(), o[a].contiguous(), lse[a].contiguous(), mode,
-                              scale)
+                g = block_bwd(do[a], q[a], ks[b].contiguous(), vs[b].contiguous(), o[a], lse[a],
+                              mode, scale)
                 dqs[a].add_(g[0].float())
-                dks[b].add_(g[1].float())
-                dvs[b].add_(g[2].float())
-        # the dK/dV accumulator follows its K/V block; after the last step it
-        # makes one more hop, which brings every block's gradients home
-        if world > 1:
-            recv_dkv, reqs = _exchange(dkv, group, rank, world)
-            for r in reqs:
-                r.wait()
-            dkv = recv_dkv
+                pks[b].add_(g[1].float())
+                pvs[b].add_(g[2].float())
+        if dkv_in is not None:
+            recvs, works = dkv_in
+            _finish(works)
+            part_k.add_(recvs[0])
+            part_v.add_(recvs[1])
+        # send the accumulator on (after the last step this hop brings every
+        # block's gradients back to its owner)
+        dkv_in = _exchange((part_k, part_v), group, rank, world) if world > 1 else \
+            ([part_k, part_v], [])
         if pending is not None:
-            recv, reqs = pending
-            for r in reqs:
-                r.wait()
-            kv = recv
-    return dq.to(q2.dtype), dkv[0].to(k2.dtype), dkv[1].to(v2.dtype)
+            recvs, works = pending
+            _finish(works)
+            kv = tuple(recvs)
+    recvs, works = dkv_in
+    _finish(works)
+    return dq.to(q2.dtype), recvs[0].to(k2.dtype), recvs[1].to(v2.dtype)
 
 
 class _RingFlashAttnFn(torch.autograd.Function):

@@ -36,6 +36,40 @@ def test_ring_one_rank_matches_kernel_and_oracle():
     assert maxdiff(o.detach(), full) <= TOL_O
 
 
+def test_ring_one_rank_long_sequence():
+    """The long-context length (S=131072, causal, D=128; 4 heads instead of 32 to
+    bound the run time): the ring (one rank, zigzag chunks of 65536 rows) against
+    the single-GPU kernel on the full tensor, and sampled query rows of O, LSE
+    and dQ against the exact oracle evaluated row by row."""
+    from oracle.attention_oracle import attention_rows
+    dev = torch.device("cuda", 0)
+    B, S, H, D = 1, 131072, 4, 128
+    g = torch.Generator(device=dev).manual_seed(21)
+    q, k, v, do = (torch.randn((B, S, H, D), device=dev, generator=g, dtype=torch.float16)
+                   for _ in range(4))
+    scale = 1.0 / math.sqrt(D)
+    leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+    o = ring.ring_flash_attn(*leaves, causal=True)
+    o.backward(do)
+    with torch.no_grad():
+        _, lse = ring._ring_forward(q, k, v, True, scale, None)
+    full = [t.clone().requires_grad_() for t in (q, k, v)]
+    of = flash_attn(*full, causal=True)
+    of.backward(do)
+    torch.cuda.synchronize(dev)
+    assert maxdiff(o.detach(), of.detach()) <= TOL_O
+    for a, b in zip(leaves, full):
+        assert maxdiff(a.grad, b.grad) <= TOL_GRAD
+    rows = [0, 1, 4097, 65535, 65536, 99999, S - 1]
+    for h in (0, 3):
+        sl = lambda t: t[:, :, h:h + 1].cpu()  # noqa: E731
+        o_r, lse_r, dq_r = attention_rows(sl(q), sl(k), sl(v), 0, 0, rows, causal=True,
+                                          scale=scale, do=sl(do))
+        assert maxdiff(o.detach()[0, rows, h].cpu(), o_r) <= TOL_O
+        assert maxdiff(lse[0, h, rows].cpu(), lse_r) <= 2e-3
+        assert maxdiff(leaves[0].grad[0, rows, h].cpu(), dq_r) <= TOL_GRAD
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

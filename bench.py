@@ -195,14 +195,33 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------- CPU path
-def cpu_pair_step(S, D, causal, amp, seed=0):
-    """One fwd+bwd of one (batch, head) pair through the CPU oracle (fp32)."""
+def cpu_reference():
+    """The reference's own CPU attention (flash_attn_volta/ref.py:9-36,
+    attention_ref) from the unmodified package installed in baseline/_ref, loaded
+    as a single module (its package __init__ would import the Triton kernels);
+    else this repo's oracle restatement of it.  Returns (fn, kind) with
+    fn(q, k, v, causal) -> fp32 output."""
+    path = os.path.join(ROOT, "baseline", "_ref", "flash_attn_volta", "ref.py")
+    if os.path.exists(path):
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_fav_reference_ref", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return (lambda q, k, v, causal: mod.attention_ref(q, k, v, causal=causal,
+                                                           dtype_out=torch.float32)), "reference"
     from oracle.attention_oracle import attention_fwd
+    return (lambda q, k, v, causal: attention_fwd(q, k, v, causal=causal,
+                                                  dtype=torch.float32)[0]), "port"
+
+
+def cpu_pair_step(fn, S, D, causal, amp, seed=0):
+    """One fwd+bwd of one (batch, head) pair through the CPU reference (fp32
+    leaves made from seeded fp16 inputs, as the reference's tests do)."""
     g = torch.Generator().manual_seed(seed)
     q, k, v, do = [(torch.randn((1, S, 1, D), generator=g) * amp).half() for _ in range(4)]
     leaves = [t.float().requires_grad_() for t in (q, k, v)]
     t0 = time.perf_counter()
-    o, _ = attention_fwd(*leaves, causal=causal, dtype=torch.float32)
+    o = fn(*leaves, causal)
     o.backward(do.float())
     return time.perf_counter() - t0
 
@@ -219,33 +238,46 @@ def cpu_model():
     return None
 
 
+CPU_PAIRS = 8  # (batch, head) pairs per CPU sample, extrapolated by FLOPs
+
+
 def cpu_baseline(S, D, causal, amp, budget_s=20.0):
+    """Median over up to 3 samples of CPU_PAIRS (b, h) pairs each (about 10-30 s
+    of CPU work at S=8192), after one warm-up pair."""
     torch.set_num_threads(os.cpu_count() or 1)
-    cpu_pair_step(min(S, 1024), D, causal, amp)  # warm-up
+    fn, kind = cpu_reference()
+    cpu_pair_step(fn, min(S, 1024), D, causal, amp)  # warm-up
     times = []
     t_start = time.perf_counter()
-    while not times or (time.perf_counter() - t_start < budget_s and len(times) < 5):
-        times.append(cpu_pair_step(S, D, causal, amp, seed=len(times)))
+    while not times or (time.perf_counter() - t_start < budget_s and len(times) < 3):
+        times.append(sum(cpu_pair_step(fn, S, D, causal, amp, seed=100 * len(times) + p)
+                         for p in range(CPU_PAIRS)))
     t = statistics.median(times)
-    f = 2.5 * flops_fwd(1, S, 1, D, causal)
+    f = CPU_PAIRS * 2.5 * flops_fwd(1, S, 1, D, causal)
     return {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port", "cpu_model": cpu_model(),
-            "sample": f"{len(times)} x fwd+bwd of one (batch, head) pair, S={S}, D={D}, "
-                      f"causal={causal}, fp32 oracle (ref.py eager restated), median "
-                      f"{t:.3f} s per pair"}
+            "kind": kind, "cpu_model": cpu_model(),
+            "sample": f"median of {len(times)} samples, each fwd+bwd of {CPU_PAIRS} (batch, head) "
+                      f"pairs, S={S}, D={D}, causal={causal}, fp32 "
+                      f"({'flash_attn_volta/ref.py attention_ref + autograd' if kind == 'reference' else 'oracle restatement of ref.py'}), "
+                      f"{t:.2f} s per sample; extrapolated to the workload by FLOPs"}
 
 
 def run_reference(args, wl):
+    """The driver's reference arm: the reference's CPU path on this host's cores,
+    each step fwd+bwd of CPU_PAIRS (batch, head) pairs of the workload."""
     world, rank, _ = dist_env()
     B, S, H, D, causal, amp = WORKLOADS[wl]
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
+    fn, kind = cpu_reference()
+    step = lambda i: sum(cpu_pair_step(fn, S, D, causal, amp, seed=CPU_PAIRS * i + p)  # noqa: E731
+                         for p in range(CPU_PAIRS))
     for i in range(args.warmup):
-        cpu_pair_step(S, D, causal, amp, seed=100 + i)
-    times = [cpu_pair_step(S, D, causal, amp, seed=i) for i in range(args.steps)]
+        step(1000 + i)
+    times = [step(i) for i in range(args.steps)]
     t = sum(times)
-    f = 2.5 * flops_fwd(1, S, 1, D, causal) * len(times)
+    f = CPU_PAIRS * 2.5 * flops_fwd(1, S, 1, D, causal) * len(times)
     val = f / t / 1e12
     line = {
         "impl": "reference", "metric": "attention fwd+bwd TFLOP/s", "value": val,
@@ -253,11 +285,11 @@ def run_reference(args, wl):
         "ms_per_step": 1e3 * t / len(times), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl, "B": B, "S": S, "H": H, "D": D, "causal": causal,
-                   "step": "fwd+bwd of one (batch, head) pair on the host CPU",
+                   "step": f"fwd+bwd of {CPU_PAIRS} (batch, head) pairs on the host CPU",
                    "l2": "n/a (CPU)"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "cpu_model": cpu_model(),
-                         "sample": f"{len(times)} steps x one (b,h) pair, S={S}, D={D}"},
+                         "kind": kind, "cpu_model": cpu_model(),
+                         "sample": f"{len(times)} steps x {CPU_PAIRS} (b,h) pairs, S={S}, D={D}"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -309,9 +341,11 @@ def run_ours(args, wl):
     q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
     stream = torch.cuda.current_stream(dev)
 
+    det = True if args.deterministic else None
+
     def step():
         q.grad = k.grad = v.grad = None
-        out = flash_attn(q, k, v, causal=causal)
+        out = flash_attn(q, k, v, causal=causal, deterministic=det)
         out.backward(do)
 
     torch.cuda.synchronize(dev)
@@ -375,7 +409,8 @@ def run_ours(args, wl):
                               "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                               "warmup": args.warmup, "ms_per_step": ms / args.steps,
                               "config": {"workload": wl, "B": B, "S": S, "H": H, "D": D,
-                                         "causal": causal, "l2": l2_note},
+                                         "causal": causal, "l2": l2_note,
+                                         "deterministic": bool(args.deterministic)},
                               "kernels_only": True}), flush=True)
         if world > 1:
             dist.destroy_process_group()
@@ -849,22 +884,79 @@ def run_ring(args):
         dist.destroy_process_group()
 
 
+def run_reference_triton(args):
+    """Informational leg (not the driver's reference arm): the unmodified
+    reference package, installed into baseline/_ref, run on this B200 through its
+    own public API (flash_attn_volta.flash_attn: Triton kernels written for
+    sm_70, compiled by the installed Triton) at the config-3 shapes, fwd+bwd,
+    L2 flushed before each step; its outputs are compared with this library's."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    dev = torch.device("cuda", 0)
+    line = {"impl": "reference-triton", "metric": "attention fwd+bwd TFLOP/s", "unit": "TFLOP/s",
+            "higher_is_better": True, "n_gpus": 1, "data": "synthetic"}
+    try:
+        sys.path.insert(0, ref_dir)
+        import flash_attn_volta as ref  # noqa: F401
+        import triton
+        line["triton"] = triton.__version__
+        from flash_attn_volta_b200 import flash_attn as ours
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        res = {}
+        for wl in ("c3a", "c3b"):
+            B, S, H, D, causal, amp = WORKLOADS[wl]
+            q, k, v, do = gen_shard(0, B, S, H, D, amp, dev)
+            outs = {}
+            for name, fn in (("reference", ref.flash_attn), ("ours", ours)):
+                qq, kk, vv = (t.clone().requires_grad_() for t in (q, k, v))
+                fn(qq, kk, vv, causal=causal).backward(do)  # compile / autotune
+                ts = []
+                for i in range(3 + max(args.steps, 5)):
+                    qq.grad = kk.grad = vv.grad = None
+                    flush.zero_()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    o = fn(qq, kk, vv, causal=causal)
+                    o.backward(do)
+                    e1.record()
+                    e1.synchronize()
+                    if i >= 3:
+                        ts.append(e0.elapsed_time(e1))
+                outs[name] = (o.detach(), qq.grad, kk.grad, vv.grad, statistics.median(ts))
+            f = 2.5 * flops_fwd(B, S, H, D, causal)
+            r, o_ = outs["reference"], outs["ours"]
+            res[wl] = {"B": B, "S": S, "H": H, "D": D, "causal": causal,
+                       "reference_ms": r[4], "reference_tflops": f / (r[4] * 1e-3) / 1e12,
+                       "ours_ms": o_[4], "ours_tflops": f / (o_[4] * 1e-3) / 1e12,
+                       "max_abs_diff": {n: float((a.float() - b.float()).abs().max())
+                                        for n, a, b in zip(("o", "dq", "dk", "dv"), r[:4], o_[:4])}}
+        line["results"] = res
+        line["value"] = res["c3b"]["reference_tflops"]
+    except Exception as e:  # compile errors of the sm_70 kernels are the result here
+        line["unavailable"] = f"{type(e).__name__}: {str(e).splitlines()[0][:300] if str(e) else ''}"
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5", "c5long"], default="c4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--soak-s", type=float, default=1.0,
                     help="seconds of untimed steps between the warm-up and the timed steps")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="time the step with the deterministic backward (dQ kernel)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="run only the warm-up and timed steps (for ncu launch lists)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args, args.workload)
+    elif args.impl == "reference-triton":
+        run_reference_triton(args)
     elif args.workload == "c5":
         run_c5(args)
     elif args.workload == "c5long":

@@ -61,7 +61,8 @@ L2_BYTES = 126 * 1000 * 1000
 # workload's whole batch, from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
 # and where it came from; the summaries are under profiles/.
 BWD_TRAFFIC_PER_LAUNCH = {
-    "c4": (5.02e9, "ncu, one launch of the p8k case (1/16 of c4's (batch, head) pairs) x 16"),
+    "c4": (5.76e9, "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full c4 launch "
+                   "(3.48 GB + 2.28 GB, 1 pass; profiles/traffic_c4_fwd_bwd_main.md)"),
 }
 
 

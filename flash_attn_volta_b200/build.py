@@ -19,7 +19,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libfa_sm100.so"
-SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_bwd_dq.cu", "fa_bwd_noalloc.cu"]
+SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_bwd_dq.cu", "fa_merge.cu", "fa_bwd_noalloc.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",

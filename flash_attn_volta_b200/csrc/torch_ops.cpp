@@ -4,6 +4,7 @@
 //   torch.ops.fav.bwd(dout, q, k, v, out, lse, causal, sm_scale, deterministic=False)
 //       -> (dq, dk, dv)
 //   torch.ops.fav.status(device) -> the device's int32 status word
+//   torch.ops.fav.merge_(acc_o, acc_lse, o, lse, first)  (ring: in-place LSE merge)
 //
 // These are the only callers of the C core on the Python side
 // (flash_attn_volta_b200/forward.py, backward.py, autograd.py): the
@@ -136,6 +137,23 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> bwd_cuda(
   return {dq, dk, dv};
 }
 
+void merge_cuda(at::Tensor& acc_o, at::Tensor& acc_lse, const at::Tensor& o_in,
+                const at::Tensor& lse_in, bool first) {
+  TORCH_CHECK(acc_o.scalar_type() == at::kFloat && acc_o.is_contiguous(),
+              "acc_o must be contiguous fp32");
+  TORCH_CHECK(acc_lse.scalar_type() == at::kFloat && acc_lse.is_contiguous(),
+              "acc_lse must be contiguous fp32");
+  const at::Tensor o = kernel_input(o_in, "o");
+  const at::Tensor lse = lse_in.contiguous();
+  TORCH_CHECK(o.sizes() == acc_o.sizes(), "o and acc_o must have the same shape");
+  c10::cuda::CUDAGuard guard(o.device());
+  const int rc = fa_sm100_merge(acc_o.data_ptr<float>(), acc_lse.data_ptr<float>(), o.data_ptr(),
+                                lse.data_ptr<float>(), (int)o.size(0), (int)o.size(1),
+                                (int)o.size(2), (int)o.size(3), dtype_code(o), first ? 1 : 0,
+                                at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc, "fa_sm100_merge");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(fav, m) {
@@ -144,9 +162,11 @@ TORCH_LIBRARY(fav, m) {
       "bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor out, Tensor lse, bool causal, "
       "float sm_scale, bool deterministic=False) -> (Tensor, Tensor, Tensor)");
   m.def("status(int device) -> Tensor", &status_word);
+  m.def("merge_(Tensor(a!) acc_o, Tensor(b!) acc_lse, Tensor o, Tensor lse, bool first) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(fav, CUDA, m) {
   m.impl("fwd", &fwd_cuda);
   m.impl("bwd", &bwd_cuda);
+  m.impl("merge_", &merge_cuda);
 }

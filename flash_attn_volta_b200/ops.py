@@ -49,6 +49,10 @@ def _register_python_parts() -> None:
     def _bwd_fake(dout, q, k, v, out, lse, causal, sm_scale, deterministic=False):
         return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
 
+    @torch.library.register_fake("fav::merge_")
+    def _merge_fake(acc_o, acc_lse, o, lse, first):
+        return None
+
     def _setup(ctx, inputs, output):
         q, k, v, causal, sm_scale = inputs
         out, lse = output

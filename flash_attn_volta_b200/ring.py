@@ -35,6 +35,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from . import ops
 from .backward import flash_attn_backward
 from .forward import flash_attn_forward
 
@@ -84,8 +85,9 @@ def _block_mode(i: int, j: int, causal: bool):
     return j == i
 
 
-def _merge(acc_o, acc_lse, o, lse):
-    """Merge a block's (o (B,C,H,D), lse (B,H,C)) into the fp32 running result."""
+def _merge_eager(acc_o, acc_lse, o, lse):
+    """The merge in plain torch operations, for CPU tensors (the gloo tests,
+    whose blocks come from the oracle)."""
     o = o.float()
     if acc_o is None:
         return o, lse.clone()
@@ -93,6 +95,20 @@ def _merge(acc_o, acc_lse, o, lse):
     w_old = torch.exp(acc_lse - new).transpose(1, 2).unsqueeze(-1)
     w_new = torch.exp(lse - new).transpose(1, 2).unsqueeze(-1)
     return acc_o * w_old + o * w_new, new
+
+
+def _merge(acc_o, acc_lse, o, lse):
+    """Merge a block's (o (B,C,H,D), lse (B,H,C)) into the fp32 running result:
+    one fa_sm100_merge kernel on the GPU (in place), plain torch on the CPU."""
+    if o.device.type != "cuda":
+        return _merge_eager(acc_o, acc_lse, o, lse)
+    first = acc_o is None
+    if first:
+        acc_o = torch.empty(o.shape, dtype=torch.float32, device=o.device)
+        acc_lse = torch.empty(lse.shape, dtype=torch.float32, device=o.device)
+    ops.load()
+    torch.ops.fav.merge_(acc_o, acc_lse, o, lse, first)
+    return acc_o, acc_lse
 
 
 def _peers(group, rank: int, world: int):
@@ -181,9 +197,10 @@ def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
                     continue
                 g = block_bwd(do[a], q[a], ks[b].contiguous(), vs[b].contiguous(), o[a], lse[a],
                               mode, scale)
-                dqs[a].add_(g[0].float())
-                pks[b].add_(g[1].float())
-                pvs[b].add_(g[2].float())
+                # fp32 += element type in one kernel each (no converted copy)
+                dqs[a].add_(g[0])
+                pks[b].add_(g[1])
+                pvs[b].add_(g[2])
         if dkv_in is not None:
             recvs, works = dkv_in
             _finish(works)

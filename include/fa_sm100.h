@@ -147,6 +147,17 @@ int fa_sm100_bwd_noalloc(const void* dout, const void* q, const void* k, const v
                          int batch, int seqlen, int nheads, int head_dim, float sm_scale,
                          int causal, int* status, void* stream);
 
+/* Merge of a partial attention result into a running one (ring context
+ * parallelism: the attention of a query chunk over one more key chunk):
+ *   lse_acc' = log(exp(lse_acc) + exp(lse)),
+ *   acc_o'   = acc_o * exp(lse_acc - lse_acc') + o * exp(lse - lse_acc').
+ * acc_o fp32 and o (dtype) are (batch, seqlen, nheads, head_dim), 16-byte
+ * aligned; lse_acc, lse are (batch, nheads, seqlen) fp32.  An lse of +inf (a
+ * row with no visible key) adds nothing.  first != 0: acc_o = o, lse_acc = lse.
+ * No counterpart in the reference (it has no multi-GPU path). */
+int fa_sm100_merge(float* acc_o, float* acc_lse, const void* o, const float* lse, int batch,
+                   int seqlen, int nheads, int head_dim, int dtype, int first, void* stream);
+
 /* Upper bound, in nanoseconds, of every on-device wait of later launches
  * (default 4e9).  Process-wide. */
 void fa_sm100_set_wait_timeout_ns(uint64_t ns);

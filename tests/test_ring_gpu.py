@@ -36,6 +36,27 @@ def test_ring_one_rank_matches_kernel_and_oracle():
     assert maxdiff(o.detach(), full) <= TOL_O
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_merge_kernel_matches_eager_merge(dtype):
+    """fa_sm100_merge (torch.ops.fav.merge_) against the plain-torch merge, three
+    blocks in a row, including rows whose block LSE is +inf (no visible key)."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    B, C, H, D = 2, 300, 3, 64
+    acc_o = acc_lse = ref_o = ref_lse = None
+    for i in range(3):
+        o = torch.randn((B, C, H, D), device=dev, generator=g).to(dtype)
+        lse = torch.randn((B, H, C), device=dev, generator=g) * 3
+        if i == 1:
+            lse[:, :, :7] = float("inf")
+        acc_o, acc_lse = ring._merge(acc_o, acc_lse, o, lse)
+        lse_e = torch.where(torch.isposinf(lse), torch.full_like(lse, float("-inf")), lse)
+        ref_o, ref_lse = ring._merge_eager(ref_o, ref_lse, o, lse_e)
+    torch.cuda.synchronize(dev)
+    assert torch.allclose(acc_lse, ref_lse, atol=1e-5, rtol=1e-5)
+    assert torch.allclose(acc_o, ref_o, atol=1e-5, rtol=1e-4)
+
+
 def test_ring_one_rank_long_sequence():
     """The long-context length (S=131072, causal, D=128; 4 heads instead of 32 to
     bound the run time): the ring (one rank, zigzag chunks of 65536 rows) against

@@ -322,11 +322,10 @@ def run_ours(args, wl):
     torch.cuda.set_device(dev)
     B, S, H, D, causal, amp = WORKLOADS[wl]
     assert B % world == 0, f"batch {B} not divisible by {world} GPUs"
-    # The headline config is timed first, in a clean process: after the large
-    # workload's allocations the same small step measured ~20 % slower, while
-    # right after 15 s of full-power load in a clean process it did not slow
-    # down (so not a clock effect; emptying the allocator cache recovered a
-    # quarter of the gap).
+    # The headline config is timed first: right after the large workload the
+    # SM clock stays in the power-capped state (1672 vs 1965 MHz, measured with
+    # NVML) for a few seconds and the same small step takes ~20 % longer.  Its
+    # own clock samples are reported beside it.
     headline = None
     if rank == 0 and world == 1 and wl != "c3b" and not args.kernels_only:
         hl_clocks = ClockSampler(local)

@@ -16,14 +16,15 @@
 // dS warps copy all of their columns to registers and release them at once, so the next
 // key block's S and dP MMAs run during the math), dS [256,384) as element-type
 // pairs in two buffers of 64 columns (the A operand of dQ += dS K), dQ
-// [384, 384+D).  Warp roles:
-//   warps 0-7  dS: warp w owns TMEM lane quarter w % 4 (query rows 32*(w%4)..)
-//              and half w / 4 of the 128 key columns.  The row's LSE and delta
-//              are per-thread scalars.  Epilogue: dQ * scale -> (B, S, H, D).
-//   warp 8     TMA producers: lane 0 Q and dO of each tile, then the K ring;
+// [384, 384+D).  Warp roles (G = kDqColGroups):
+//   warps 0..4G-1  dS: warp w owns TMEM lane quarter w % 4 (query rows
+//              32*(w%4)..) and key-column group w / 4 (128 / G columns).  The
+//              row's LSE and delta are per-thread scalars.  Epilogue: dQ *
+//              scale -> (B, S, H, D).
+//   warp 4G    TMA producers: lane 0 Q and dO of each tile, then the K ring;
 //              lane 1 the V ring.
-//   warp 9     S = Q K^T and dP = dO V^T (both operands in shared memory).
-//   warp 10    dQ += dS K (dS from tensor memory, K from shared memory).
+//   warp 4G+1  S = Q K^T and dP = dO V^T (both operands in shared memory).
+//   warp 4G+2  dQ += dS K (dS from tensor memory, K from shared memory).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,13 +37,29 @@
 
 namespace fa_sm100 {
 
+// dS warps: 4 x kDqColGroups (each a TMEM lane quarter x 128 / kDqColGroups key columns)
+#ifndef FA_DQ_COL_GROUPS
+#define FA_DQ_COL_GROUPS 2
+#endif
+constexpr int kDqColGroups = FA_DQ_COL_GROUPS;
+constexpr int kDqSoftWarps = 4 * kDqColGroups;
+#ifndef FA_DQ_NSTK_SMALL
+#define FA_DQ_NSTK_SMALL 3
+#endif
+
+
 template <int D>
 struct DqCfg {
   static constexpr int BM = 128, BN = 128;                  // query rows, key rows per step
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle width (bytes)
   static constexpr int AE = SWB / 2;
   static constexpr int NAT = D / AE;
-  static constexpr int NSTK = (D == 128) ? 2 : 3;  // K ring depth
+  // K ring depth.  A K stage is read twice, by S of its block and by dQ += dS K,
+  // which runs only after that block's dS: with two stages the load of block
+  // j + 2 waited for dQ(j) and its latency stalled S(j + 2) (measured at D=128:
+  // 3 stages took the deterministic backward 16.0 -> 15.1 ms at B=8, S=8192,
+  // H=32 and 138 -> 126 us at B=1, S=4096, H=8).
+  static constexpr int NSTK = (D == 128) ? 3 : FA_DQ_NSTK_SMALL;
   static constexpr int NSTV = (D == 128) ? 2 : 3;  // V ring depth
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
@@ -53,7 +70,8 @@ struct DqCfg {
   static constexpr int OFF_BAR = OFF_V + NSTV * KV_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers, TMEM slot, abort flag + slack
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 352;
+  static_assert(NSTK <= 5 && NSTV <= 3, "barrier slots of the K / V rings");
+  static constexpr int THREADS = (kDqSoftWarps + 3) * 32;  // + TMA, S/dP issuer, dQ issuer
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DS = 256, COL_DQ = 384;
 };
@@ -61,22 +79,22 @@ struct DqCfg {
 enum DqBar {
   Q_FULL = 0,
   Q_EMPTY = 1,   // a tile's last S and dP MMAs have read Q and dO
-  K_FULL = 2,    // +NSTK (<= 3)
-  K_EMPTY = 5,   // +NSTK: dQ += dS K of that block done
-  V_FULL = 8,    // +NSTV (<= 3)
-  V_EMPTY = 11,  // +NSTV
-  S_FULL = 14,   // S and dP of a key block complete
-  S_FREE = 15,   // 8 arrivals: S and dP copied to registers
-  DS_FULL = 16,  // +b, 8 arrivals: dS_b written
-  DS_FREE = 18,  // +b: dQ += dS_b K done reading dS_b
-  DQ_DONE = 20,  // a tile's last dQ MMA complete
-  DQ_FREE = 21,  // 8 arrivals: the epilogue has read dQ
-  DQ_DRAIN = 22, // 2 arrivals: each issuer's last commit
-  DQ_BAR_COUNT = 23
+  K_FULL = 2,    // +NSTK (<= 5)
+  K_EMPTY = 7,   // +NSTK: dQ += dS K of that block done
+  V_FULL = 12,   // +NSTV (<= 3)
+  V_EMPTY = 15,  // +NSTV
+  S_FULL = 18,   // S and dP of a key block complete
+  S_FREE = 19,   // all dS warps: S and dP copied to registers
+  DS_FULL = 20,  // +b, all dS warps: dS_b written
+  DS_FREE = 22,  // +b: dQ += dS_b K done reading dS_b
+  DQ_DONE = 24,  // a tile's last dQ MMA complete
+  DQ_FREE = 25,  // all dS warps: the epilogue has read dQ
+  DQ_DRAIN = 26, // 2 arrivals: each issuer's last commit
+  DQ_BAR_COUNT = 27
 };
 
 template <int D, typename T>
-__global__ void __launch_bounds__(352, 1)
+__global__ void __launch_bounds__((kDqSoftWarps + 3) * 32, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -126,14 +144,14 @@ __global__ void __launch_bounds__(352, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < DQ_BAR_COUNT; ++i) {
       uint32_t cnt = 1;
-      if (i == S_FREE || i == DS_FULL || i == DS_FULL + 1 || i == DQ_FREE) cnt = 8;
+      if (i == S_FREE || i == DS_FULL || i == DS_FULL + 1 || i == DQ_FREE) cnt = kDqSoftWarps;
       if (i == DQ_DRAIN) cnt = 2;
       mbar_init(bar(i), cnt);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kDqSoftWarps + 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -146,7 +164,7 @@ __global__ void __launch_bounds__(352, 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  if (warp == 8) {
+  if (warp == kDqSoftWarps) {
     // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -213,7 +231,7 @@ __global__ void __launch_bounds__(352, 1)
           mbar_wait_drain(bar(V_FULL + g % C::NSTV), (uint32_t)(g / C::NSTV) & 1u, timeout_ns);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kDqSoftWarps + 1) {
     // ------------------------------------------------------------ S / dP issuer
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
@@ -265,7 +283,7 @@ __global__ void __launch_bounds__(352, 1)
       }
       mma_commit(bar(DQ_DRAIN));  // also on abort: teardown waits for every issued MMA
     }
-  } else if (warp == 10) {
+  } else if (warp == kDqSoftWarps + 2) {
     // ------------------------------------------------------------ dQ issuer
     if (lane == 0) {
       constexpr uint32_t swz = swizzle_field(C::SWB);
@@ -302,13 +320,15 @@ __global__ void __launch_bounds__(352, 1)
       }
       mma_commit(bar(DQ_DRAIN));
     }
-  } else if (warp < 8) {
-    // ------------------------------------------------------------ dS warps 0..7
+  } else if (warp < kDqSoftWarps) {
+    // ------------------------------------------------------------ dS warps
+    constexpr int CPW = C::BN / kDqColGroups;  // key columns per warp
+    constexpr int NCH = CPW / 32;              // 32-column chunks per warp
     const int lq = warp & 3, hf = warp >> 2;
     const int r = lq * 32 + lane;  // query row inside the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-    const int c0 = hf * 64;        // first key column of this thread
-    constexpr int EC = (D / 2 >= 16) ? D / 2 : 16;  // dQ epilogue columns per warp
+    const int c0 = hf * CPW;       // first key column of this thread
+    constexpr int EC = (D / kDqColGroups >= 16) ? D / kDqColGroups : 16;  // dQ epilogue columns per warp
     const float INF = __int_as_float(0x7f800000);
     bool ok = true;
     int gs = 0, nt = 0;
@@ -337,19 +357,20 @@ __global__ void __launch_bounds__(352, 1)
         const int kv0 = j * C::BN;
         // every (query, key) pair of this block is unmasked
         const bool full = (kv0 + C::BN <= Sk) && (!causal || kv0 + C::BN - 1 <= tl.q0 + off);
-        // all 64 columns of S and dP into registers, then release them at once
-        // (the next key block's S and dP MMAs run during the math below)
-        uint32_t sr[2][32], dr[2][32];
-        tmem_ld32(tmem + lane_base + C::COL_S + c0, sr[0]);
-        tmem_ld32(tmem + lane_base + C::COL_DP + c0, dr[0]);
-        tmem_ld32(tmem + lane_base + C::COL_S + c0 + 32, sr[1]);
-        tmem_ld32(tmem + lane_base + C::COL_DP + c0 + 32, dr[1]);
+        // all of this thread's columns of S and dP into registers, then release
+        // them at once (the next key block's S and dP MMAs run during the math)
+        uint32_t sr[NCH][32], dr[NCH][32];
+#pragma unroll
+        for (int cc = 0; cc < NCH; ++cc) {
+          tmem_ld32(tmem + lane_base + C::COL_S + c0 + cc * 32, sr[cc]);
+          tmem_ld32(tmem + lane_base + C::COL_DP + c0 + cc * 32, dr[cc]);
+        }
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(S_FREE));
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
+        for (int cc = 0; cc < NCH; ++cc) {
           const int cb = c0 + cc * 32;  // first key column of this chunk
           uint32_t dd[16];
           if (full) {
@@ -433,7 +454,7 @@ __global__ void __launch_bounds__(352, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kDqSoftWarps + 1) {
     if (lane == 0) mbar_wait_drain(bar(DQ_DRAIN), 0, timeout_ns);
     __syncwarp();
     tc_fence_after();

@@ -17,12 +17,15 @@ kernels:
   O = sum_j exp(lse_ij - lse) O_ij in fp32 (each O_ij arrives rounded to the
   element type by the kernel).  The next K and V blocks are exchanged (one
   batched isend/irecv to r+1 / from r-1) while the current one is computed.
-* Backward: the same ring; each block's (dq, dk, dv) come from the single-GPU
-  backward fed with the *final* O and LSE (so P and delta are the global ones,
-  as in the reference's Algorithm-4 backward); dq accumulates locally and
-  dk/dv accumulate in fp32 buffers that travel with their K/V block and make
-  one last hop back to their owner.  A step's contribution is computed into a
-  fresh buffer while the accumulator arrives, so that hop overlaps compute too.
+* Backward: the same K/V ring; each block's (dq, dk, dv) come from the
+  single-GPU backward fed with the *final* O and LSE (so P and delta are the
+  global ones, as in the reference's Algorithm-4 backward); dq accumulates
+  locally.  A step's dK/dV contributions go straight to the owner of that
+  K/V block (rank - step), in the kernels' element type and only for the key
+  chunks the step's queries attend to, and the owner accumulates them in fp32:
+  under the zigzag causal layout about half of the steps touch one key chunk
+  only, so this moves ~3x fewer bytes than an fp32 accumulator travelling
+  with its block.  The transfer of step s overlaps the compute of step s + 1.
 
 Received blocks land in local buffers before a kernel reads them: no kernel
 touches another GPU's memory.
@@ -167,6 +170,15 @@ def _ring_forward(q2, k2, v2, causal, scale, group):
     return o, lse
 
 
+def _contributions(q_rank: int, k_rank: int, world: int, causal: bool) -> list:
+    """Key chunks (0 / 1) of rank k_rank that the query chunks of rank q_rank
+    attend to: the dK / dV chunks a backward step of q_rank on k_rank's block
+    contributes to (the same on the sending and the receiving side)."""
+    ids_q, ids_k = zigzag_chunk_ids(q_rank, world), zigzag_chunk_ids(k_rank, world)
+    return [b for b in range(2)
+            if any(_block_mode(ids_q[a], ids_k[b], causal) is not None for a in range(2))]
+
+
 def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
     rank, world = _world(group)
     q = [c.contiguous() for c in q2.chunk(2, dim=1)]
@@ -176,20 +188,23 @@ def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
     ids_q = zigzag_chunk_ids(rank, world)
     dq = torch.zeros(q2.shape, dtype=torch.float32, device=q2.device)
     dqs = dq.chunk(2, dim=1)
+    # dK / dV of this rank's own K/V block, accumulated here in fp32.  At step s
+    # this rank computes the contributions of its queries to block src = rank - s
+    # and sends them straight to that block's owner, in the kernels' element
+    # type (which their outputs are rounded to already; two contributions to
+    # one chunk are summed in fp32 first) and only for the key chunks its
+    # queries attend to.  The owner receives from rank + s at the same step.
+    dk_acc = torch.zeros(k2.shape, dtype=torch.float32, device=q2.device)
+    dv_acc = torch.zeros(v2.shape, dtype=torch.float32, device=q2.device)
+    dks_acc, dvs_acc = dk_acc.chunk(2, dim=1), dv_acc.chunk(2, dim=1)
     kv = (k2, v2)
-    # dK / dV of the K/V block a rank holds travel with it, in fp32.  At step s
-    # the accumulator of block (rank - s) arrives from rank-1 while this rank
-    # computes that block's contribution into a fresh buffer; the two are added
-    # once both are there and sent on, so the hop overlaps the next step.
-    dkv_in = None  # (recvs, works) of the accumulator arriving for this step's block
+    inflight = None  # (works, recv tensors, chunk ids, send tensors kept alive)
     for step in range(world):
         src = (rank - step) % world
         ids_k = zigzag_chunk_ids(src, world)
         pending = _exchange(kv, group, rank, world) if step < world - 1 else None
         ks, vs = kv[0].chunk(2, dim=1), kv[1].chunk(2, dim=1)
-        part_k = torch.zeros(k2.shape, dtype=torch.float32, device=q2.device)
-        part_v = torch.zeros(v2.shape, dtype=torch.float32, device=q2.device)
-        pks, pvs = part_k.chunk(2, dim=1), part_v.chunk(2, dim=1)
+        part = {}  # key chunk -> [dk, dv] (fp32 once a second contribution arrives)
         for a in range(2):
             for b in range(2):
                 mode = _block_mode(ids_q[a], ids_k[b], causal)
@@ -197,26 +212,48 @@ def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
                     continue
                 g = block_bwd(do[a], q[a], ks[b].contiguous(), vs[b].contiguous(), o[a], lse[a],
                               mode, scale)
-                # fp32 += element type in one kernel each (no converted copy)
-                dqs[a].add_(g[0])
-                pks[b].add_(g[1])
-                pvs[b].add_(g[2])
-        if dkv_in is not None:
-            recvs, works = dkv_in
+                dqs[a].add_(g[0])  # fp32 += element type in one kernel
+                if b in part:
+                    part[b] = [part[b][0].float().add_(g[1]), part[b][1].float().add_(g[2])]
+                else:
+                    part[b] = [g[1], g[2]]
+        if inflight is not None:
+            works, recvs, chunks, _ = inflight
             _finish(works)
-            part_k.add_(recvs[0])
-            part_v.add_(recvs[1])
-        # send the accumulator on (after the last step this hop brings every
-        # block's gradients back to its owner)
-        dkv_in = _exchange((part_k, part_v), group, rank, world) if world > 1 else \
-            ([part_k, part_v], [])
+            for i, b in enumerate(chunks):
+                dks_acc[b].add_(recvs[2 * i])
+                dvs_acc[b].add_(recvs[2 * i + 1])
+            inflight = None
+        if step == 0:
+            for b, (gk, gv) in part.items():
+                dks_acc[b].add_(gk)
+                dvs_acc[b].add_(gv)
+        else:
+            dst, peer = (rank - step) % world, (rank + step) % world
+            sends = []
+            for b in sorted(part):
+                sends += [part[b][0].to(k2.dtype).contiguous(), part[b][1].to(v2.dtype).contiguous()]
+            chunks = _contributions(peer, rank, world, causal)
+            shape = ks[0].shape
+            recvs = [torch.empty(shape, dtype=k2.dtype, device=q2.device)
+                     for _ in range(2 * len(chunks))]
+            g_dst = dist.get_global_rank(group, dst) if group is not None else dst
+            g_peer = dist.get_global_rank(group, peer) if group is not None else peer
+            ops_ = [dist.P2POp(dist.isend, t, g_dst, group) for t in sends]
+            ops_ += [dist.P2POp(dist.irecv, t, g_peer, group) for t in recvs]
+            works = dist.batch_isend_irecv(ops_) if ops_ else []
+            inflight = (works, recvs, chunks, sends)
         if pending is not None:
-            recvs, works = pending
-            _finish(works)
-            kv = tuple(recvs)
-    recvs, works = dkv_in
-    _finish(works)
-    return dq.to(q2.dtype), recvs[0].to(k2.dtype), recvs[1].to(v2.dtype)
+            recvs_kv, works_kv = pending
+            _finish(works_kv)
+            kv = tuple(recvs_kv)
+    if inflight is not None:
+        works, recvs, chunks, _ = inflight
+        _finish(works)
+        for i, b in enumerate(chunks):
+            dks_acc[b].add_(recvs[2 * i])
+            dvs_acc[b].add_(recvs[2 * i + 1])
+    return dq.to(q2.dtype), dk_acc.to(k2.dtype), dv_acc.to(v2.dtype)
 
 
 class _RingFlashAttnFn(torch.autograd.Function):

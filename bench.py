@@ -333,6 +333,7 @@ def run_ours(args, wl):
         headline = bench_small("c3b", dev, args)
         headline["c3a"] = bench_small("c3a", dev, args)
         headline["host_us_per_call"] = host_cost_us(dev)
+        headline["cuda_graph"] = graph_vs_eager_us(dev)
         headline["clocks"] = hl_clocks.stop()
     mem_c3a = peak_mem_fwd_bwd(dev, 1, 4096, 16, 64, True)
     torch.cuda.empty_cache()
@@ -652,6 +653,56 @@ def host_cost_us(dev, calls=2000):
         torch.cuda.synchronize(dev)
         res[name] = 1e6 * (t1 - t0) / calls
     return res
+
+
+def graph_vs_eager_us(dev, wl="c1", reps=30):
+    """Step time (us) of a small workload's fwd+bwd through the public API,
+    eager (host cost per call included) against the same step captured once in
+    a CUDA graph and replayed; L2 flushed before each step."""
+    from flash_attn_volta_b200 import flash_attn
+    B, S, H, D, causal, amp = WORKLOADS[wl]
+    q, k, v, do = gen_shard(0, B, S, H, D, amp, dev, seed_base=77)
+    for t in (q, k, v):
+        t.requires_grad_()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        flash_attn(q, k, v, causal=causal).backward(do)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            q.grad = k.grad = v.grad = None
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    q.grad = k.grad = v.grad = None
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+
+    def timed(fn):
+        ts = []
+        for i in range(5 + reps):
+            flush.zero_()
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            if i >= 5:
+                ts.append(1e3 * e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    def eager():
+        q.grad = k.grad = v.grad = None
+        step()
+
+    return {"workload": wl, "eager_us": timed(eager), "graph_replay_us": timed(g.replay),
+            "what": "one fwd+bwd step from an idle GPU (synchronised before each step): "
+                    "eager includes the host time of the two calls"}
 
 
 def bench_small(wl, dev, args):

@@ -82,7 +82,13 @@ __device__ unsigned long long g_bcta[8192][4];
   } while (0)
 #endif
 
-template <int D>
+// Q / dO ring depth without the fused dQ path (its staging buffers free the
+// shared memory for a fourth stage)
+#ifndef FA_BWD_NST_NODQ
+#define FA_BWD_NST_NODQ 4
+#endif
+
+template <int D, bool DQ = true>
 struct BwdCfg {
   static constexpr int BN = 128;                    // key rows per CTA
   static constexpr int BM = (D == 128) ? 64 : 128;  // query rows per iteration
@@ -90,7 +96,11 @@ struct BwdCfg {
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;
   static constexpr int AE = SWB / 2;
   static constexpr int NAT = D / AE;
-  static constexpr int NST = 3;  // Q / dO (+ their extra K-step rows) ring depth
+  // Q / dO (+ their extra K-step rows) ring depth.  A stage is held until dV / dK
+  // of its query tile (after the softmax) have read it, so the load of tile
+  // i + NST waits for them; more stages hide that latency where shared memory
+  // allows.
+  static constexpr int NST = (DQ || D != 128) ? 3 : FA_BWD_NST_NODQ;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int PT_BYTES = BN * BM * 2;  // [key row][query col], 64-col atoms
@@ -110,9 +120,12 @@ struct BwdCfg {
   static constexpr int OFF_DS = OFF_P;  // P^T lives in tensor memory, not here
   static constexpr int DQ_STAGE_BYTES = BM * D * 4;  // one dQ partial, [q][d] fp32
   static constexpr int NDQ = (D <= 32) ? 2 : 1;        // dQ staging buffers
-  static constexpr int OFF_DQS = OFF_DS + PT_BYTES;
-  static constexpr int SMEM = OFF_DQS + NDQ * DQ_STAGE_BYTES + 1024;  // + alignment slack
+  // dS^T in shared memory: read by the dQ MMA, and by the dK MMA below D=128
+  static constexpr bool DS_SMEM = DQ || D != 128;
+  static constexpr int OFF_DQS = OFF_DS + (DS_SMEM ? PT_BYTES : 0);
+  static constexpr int SMEM = OFF_DQS + (DQ ? NDQ * DQ_STAGE_BYTES : 0) + 1024;  // + slack
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(NST <= 5, "barrier slots of the Q / dO ring");
   static constexpr int THREADS = 544;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = BM, COL_DQ = 2 * BM;
@@ -128,20 +141,20 @@ struct BwdCfg {
 
 enum BwdBar {
   C_KVFULL = 0,
-  C_QFULL = 1,   // +NST (<= 3)
-  C_QEMPTY = 4,  // +NST
-  C_SFULL = 7,
-  C_DPFULL = 8,
-  C_SFREE = 9,     // 8 arrivals (softmax warps hold S^T / dP^T in registers)
-  C_DSREADY = 10,  // 8 arrivals (P^T / dS^T written to shared memory)
-  C_PFREE = 11,
-  C_DQFULL = 12,
-  C_DQFREE = 13,  // 4 arrivals
-  C_KVDONE = 14,
-  C_DRAIN = 15,   // 4 arrivals: each MMA issuer's last commit
-  C_KVEMPTY = 16,  // 3 arrivals: a tile's last S^T, dP^T and dQ MMAs have read K / V
-  C_DKVFREE = 17,  // 8 arrivals: the epilogue has read dK / dV
-  C_COUNT = 18
+  C_QFULL = 1,   // +NST (<= 5)
+  C_QEMPTY = 6,  // +NST
+  C_SFULL = 11,
+  C_DPFULL = 12,
+  C_SFREE = 13,     // 8 arrivals (softmax warps hold S^T / dP^T in registers)
+  C_DSREADY = 14,  // 8 arrivals (P^T / dS^T written to shared memory)
+  C_PFREE = 15,
+  C_DQFULL = 16,
+  C_DQFREE = 17,  // 4 arrivals
+  C_KVDONE = 18,
+  C_DRAIN = 19,   // 4 arrivals: each MMA issuer's last commit
+  C_KVEMPTY = 20,  // 3 arrivals: a tile's last S^T, dP^T and dQ MMAs have read K / V
+  C_DKVFREE = 21,  // 8 arrivals: the epilogue has read dK / dV
+  C_COUNT = 22
 };
 
 // -------------------------------------------------------------------------- pre
@@ -287,7 +300,7 @@ __global__ void __launch_bounds__(544, 1)
                        int S_pad, int ntiles, int win,
                        float scale, float scale_log2, int causal, int* status,
                        unsigned long long timeout_ns) {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<D, DQ>;
   constexpr int HW = C::BM / 2;  // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -850,7 +863,7 @@ __global__ void __launch_bounds__(544, 1)
 
 template <int D, typename T, bool DQ>
 static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<D, DQ>;
   constexpr int tag = 2000 + D + (std::is_same<T, __half>::value ? 0 : 1000) + (DQ ? 0 : 4000);
   if (!smem_attr_set<tag>(reinterpret_cast<const void*>(fa_bwd_main_kernel<D, T, DQ>), C::SMEM))
     return FA_ERR_LAUNCH;

@@ -21,6 +21,8 @@ FA_ERR_DEVICE = 4
 FA_ERR_WORKSPACE = 5
 FA_ERR_SCRATCH_LIMIT = 6
 
+BWD_DETERMINISTIC = 1
+
 STATUS_TIMEOUT = 1
 STATUS_RANGE = 2
 
@@ -64,6 +66,13 @@ def load() -> ctypes.CDLL:
             lib.fa_sm100_bwd_ex.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 7 + [
                 _c_float, _c_int, _vp, _vp]
             lib.fa_sm100_bwd_ex.restype = _c_int
+            lib.fa_sm100_bwd_flags.argtypes = [_vp] * 10 + [_c_size] + [_c_int] * 7 + [
+                _c_float, _c_int, _c_int, _vp, _vp]
+            lib.fa_sm100_bwd_flags.restype = _c_int
+            lib.fa_sm100_bwd_workspace_bytes_flags.argtypes = [_c_int] * 5
+            lib.fa_sm100_bwd_workspace_bytes_flags.restype = _c_size
+            lib.fa_sm100_merge.argtypes = [_vp] * 4 + [_c_int] * 6 + [_vp]
+            lib.fa_sm100_merge.restype = _c_int
             lib.fa_sm100_bwd_phase.argtypes = [_c_int] + lib.fa_sm100_bwd.argtypes
             lib.fa_sm100_bwd_phase.restype = _c_int
             lib.fa_sm100_bwd_noalloc.argtypes = [_vp] * 9 + [_c_int] * 4 + [_c_float, _c_int,

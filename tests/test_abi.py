@@ -97,3 +97,28 @@ def test_ex_head_count_and_dtype_checks():
     assert rc == _lib.FA_ERR_ARG
     rc = lib.fa_sm100_bwd_ex(*([256] * 9), 256, n, 1, 64, 64, 8, 2, 64, 9, 0.125, 1, None, None)
     assert rc == _lib.FA_ERR_ARG
+
+
+def test_deterministic_flag_workspace_and_checks():
+    """FA_BWD_DETERMINISTIC needs no fp32 dQ accumulator; unknown flag bits are
+    refused before touching the device."""
+    lib = _lib.load()
+    B, S, H, D = 2, 1000, 4, 128
+    fused = lib.fa_sm100_bwd_workspace_bytes_flags(B, S, H, D, 0)
+    det = lib.fa_sm100_bwd_workspace_bytes_flags(B, S, H, D, _lib.BWD_DETERMINISTIC)
+    assert fused == lib.fa_sm100_bwd_workspace_bytes(B, S, H, D)
+    rows = B * H * 1024  # rows padded to 128
+    assert fused - det >= rows * D * 4 - rows * 4  # the accumulator is gone, delta is added
+    assert lib.fa_sm100_bwd_workspace_bytes_flags(B, S, H, D, 2) == 0
+    rc = lib.fa_sm100_bwd_flags(*([256] * 9), 256, fused, B, S, S, H, H, D, _lib.DTYPE_F16,
+                                0.1, 1, 2, None, None)
+    assert rc == _lib.FA_ERR_ARG
+
+
+def test_merge_argument_checks():
+    lib = _lib.load()
+    f16 = _lib.DTYPE_F16
+    assert lib.fa_sm100_merge(256, 256, 256, 256, 1, 8, 2, 48, f16, 1, None) == _lib.FA_ERR_ARG
+    assert lib.fa_sm100_merge(None, 256, 256, 256, 1, 8, 2, 64, f16, 1, None) == _lib.FA_ERR_ARG
+    assert lib.fa_sm100_merge(264, 256, 256, 256, 1, 8, 2, 64, f16, 1, None) == _lib.FA_ERR_ARG
+    assert lib.fa_sm100_merge(256, 256, 256, 256, 1, 8, 2, 64, 5, 1, None) == _lib.FA_ERR_ARG

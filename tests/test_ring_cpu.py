@@ -93,3 +93,16 @@ def test_block_backward_oracle_reduces_to_plain_backward():
     b = attention_bwd(do, q, k, v, True)
     for x, y in zip(a, b):
         assert maxdiff(x, y) < 1e-10
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_dkdv_contribution_sets(world):
+    """Which key chunks of rank k the queries of rank q reach (the dK/dV chunks
+    a backward step sends to k's owner): under the zigzag causal layout a rank
+    behind the key rank reaches only its first chunk, the others both; without a
+    causal mask always both.  Sender and receiver use the same function."""
+    for q in range(world):
+        for k in range(world):
+            want = [0] if k < q else [0, 1]
+            assert ring._contributions(q, k, world, True) == want, (q, k)
+            assert ring._contributions(q, k, world, False) == [0, 1]

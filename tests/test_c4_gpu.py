@@ -8,6 +8,9 @@ checked: the first and last batch crossed with the first and last head, plus
 four in between.  Tolerances as everywhere: O and LSE <= 2e-3, dQ / dK / dV
 <= 5e-3 max-abs.
 
+The deterministic backward is checked at this size too (sampled heads against
+the oracle, two runs bit-identical including dQ).
+
 Batch shards: `bench.py --gpus N` gives rank r the batches [r*B/N, (r+1)*B/N)
 and runs the same kernels on that slice.  O, LSE, dK and dV of a shard must
 equal, bit for bit, the same batches of the single-GPU run (dQ is summed with
@@ -86,3 +89,30 @@ def test_c4_batch_shard_bit_identical(c4_run, n_ranks, rank):
     assert torch.equal(sdk, dk[b0:b1])
     assert torch.equal(sdv, dv[b0:b1])
     assert maxdiff(sdq, dq[b0:b1]) <= 1e-3
+
+
+def test_c4_deterministic_vs_oracle_and_bit_identical(c4_run):
+    """The deterministic backward at the benchmark size: sampled heads against
+    the exact oracle, and dQ / dK / dV bit-identical over two runs (64 key
+    blocks per causal query row at S=8192)."""
+    from flash_attn_volta_b200 import check_status, flash_attn
+    (q, k, v, do), (o, lse, dq, dk, dv) = c4_run
+    runs = []
+    for _ in range(2):
+        qd, kd, vd = (t.detach().clone().requires_grad_() for t in (q, k, v))
+        flash_attn(qd, kd, vd, causal=True, deterministic=True).backward(do)
+        torch.cuda.synchronize(DEV)
+        check_status(DEV)
+        runs.append((qd.grad, kd.grad, vd.grad))
+        del qd, kd, vd
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
+    gq, gk, gv = runs[0]
+    assert torch.equal(gk, dk) and torch.equal(gv, dv)  # dK / dV: same kernel arithmetic
+    scale = 1.0 / math.sqrt(D)
+    worst = 0.0
+    for b, h in HEADS[:4]:
+        sl = lambda t: t[b:b + 1, :, h:h + 1, :].cpu()  # noqa: E731
+        ref = oracle_heads(sl(q), sl(k), sl(v), sl(do), True, scale, [(0, 0)])
+        worst = max(worst, maxdiff(gq[b, :, h].cpu(), ref["dq"][0]))
+    assert worst <= TOL_GRAD, worst

@@ -134,3 +134,28 @@ def test_deterministic_causal_no_leak_bit_identical_many_blocks():
         grads.append(qd.grad.cpu())
     assert (grads[0][:, :j] - grads[1][:, :j]).abs().max().item() == 0.0
     assert (grads[0][:, j:] - grads[1][:, j:]).abs().max().item() > 1e-3
+
+
+def test_deterministic_fully_masked_rows():
+    """Sq > Sk with the bottom-right causal mask: the first Sq - Sk query rows see
+    no key (O = 0, LSE = +inf, dQ = 0), whole 128-row query tiles among them
+    (the dQ kernel writes those tiles' zeros without any key block)."""
+    from flash_attn_volta_b200 import check_status, flash_attn
+    from oracle.attention_oracle import attention_bwd, attention_fwd
+    B, Sq, Sk, H, D = 1, 700, 200, 2, 64
+    g = torch.Generator().manual_seed(13)
+    q = torch.randn((B, Sq, H, D), generator=g).half()
+    k = torch.randn((B, Sk, H, D), generator=g).half()
+    v = torch.randn((B, Sk, H, D), generator=g).half()
+    do = torch.randn((B, Sq, H, D), generator=g).half()
+    qd, kd, vd = (t.to(DEV).requires_grad_() for t in (q, k, v))
+    out = flash_attn(qd, kd, vd, causal=True, deterministic=True)
+    out.backward(do.to(DEV))
+    torch.cuda.synchronize(DEV)
+    check_status(DEV)
+    o_ref, _ = attention_fwd(q, k, v, True, dtype=torch.float64, causal_offset=Sk - Sq)
+    dq, dk, dv = attention_bwd(do, q, k, v, True, causal_offset=Sk - Sq)
+    assert (qd.grad[:, :Sq - Sk] == 0).all() and (out[:, :Sq - Sk] == 0).all()
+    assert maxdiff(out.detach().cpu(), o_ref) <= TOL_O
+    for got, ref in ((qd.grad, dq), (kd.grad, dk), (vd.grad, dv)):
+        assert maxdiff(got.cpu(), ref) <= TOL_GRAD

@@ -52,6 +52,23 @@ at::Tensor kernel_input(const at::Tensor& t, const char* name) {
   return c;
 }
 
+// The C ABI takes every extent from q and k, so each other tensor must have
+// exactly the shape it implies, and every tensor must sit on q's device (a
+// mismatch would otherwise become an out-of-bounds or peer read on the GPU).
+void check_like(const at::Tensor& t, at::IntArrayRef sizes, const at::Tensor& q, const char* name) {
+  TORCH_CHECK(t.sizes() == sizes, name, " has shape ", t.sizes(), ", expected ", sizes);
+  TORCH_CHECK(t.device() == q.device(), name, " is on ", t.device(), ", q on ", q.device());
+}
+
+void check_qkv(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+  TORCH_CHECK(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type(),
+              "q, k, v must have the same dtype");
+  check_like(k, {q.size(0), k.size(1), k.size(2), q.size(3)}, q, "k");
+  check_like(v, k.sizes(), q, "v");
+  TORCH_CHECK(k.size(2) > 0 && q.size(2) % k.size(2) == 0,
+              "the query heads must be a multiple of the key/value heads");
+}
+
 // One int32 status word per device, created on first use (make that first
 // call before any CUDA graph capture).
 constexpr int kMaxDev = 64;
@@ -75,9 +92,7 @@ std::tuple<at::Tensor, at::Tensor> fwd_cuda(const at::Tensor& q_in, const at::Te
   const at::Tensor k = kernel_input(k_in, "k");
   const at::Tensor v = kernel_input(v_in, "v");
   const int dt = dtype_code(q);
-  TORCH_CHECK(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type(),
-              "q, k, v must have the same dtype");
-  TORCH_CHECK(k.sizes() == v.sizes(), "k and v must have the same shape");
+  check_qkv(q, k, v);
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
   c10::cuda::CUDAGuard guard(q.device());
@@ -109,10 +124,16 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> bwd_cuda(
   const at::Tensor v = kernel_input(v_in, "v");
   const at::Tensor out = kernel_input(out_in, "out");
   const int dt = dtype_code(q);
+  check_qkv(q, k, v);
+  TORCH_CHECK(dout.scalar_type() == q.scalar_type() && out.scalar_type() == q.scalar_type(),
+              "dout and out must have q's dtype");
   TORCH_CHECK(lse_in.scalar_type() == at::kFloat, "lse must be fp32");
   const at::Tensor lse = lse_in.contiguous();
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
+  check_like(dout, q.sizes(), q, "dout");
+  check_like(out, q.sizes(), q, "out");
+  check_like(lse, {B, H, Sq}, q, "lse");
   c10::cuda::CUDAGuard guard(q.device());
   at::Tensor dq = at::empty(q.sizes(), q.options());
   at::Tensor dk = at::empty(k.sizes(), k.options());
@@ -145,7 +166,10 @@ void merge_cuda(at::Tensor& acc_o, at::Tensor& acc_lse, const at::Tensor& o_in,
               "acc_lse must be contiguous fp32");
   const at::Tensor o = kernel_input(o_in, "o");
   const at::Tensor lse = lse_in.contiguous();
-  TORCH_CHECK(o.sizes() == acc_o.sizes(), "o and acc_o must have the same shape");
+  check_like(acc_o, o.sizes(), o, "acc_o");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat, "lse must be fp32");
+  check_like(lse, {o.size(0), o.size(2), o.size(1)}, o, "lse");
+  check_like(acc_lse, lse.sizes(), o, "acc_lse");
   c10::cuda::CUDAGuard guard(o.device());
   const int rc = fa_sm100_merge(acc_o.data_ptr<float>(), acc_lse.data_ptr<float>(), o.data_ptr(),
                                 lse.data_ptr<float>(), (int)o.size(0), (int)o.size(1),

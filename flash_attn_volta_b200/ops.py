@@ -39,18 +39,42 @@ def load() -> None:
         _loaded = True
 
 
+def _expect(t, shape, name):
+    if tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _check_qkv(q, k, v):
+    """The shape rules the CUDA operators enforce (csrc/torch_ops.cpp), for
+    the shape functions, so a traced call fails where an eager one would."""
+    if q.dim() != 4 or k.dim() != 4:
+        raise RuntimeError("q, k, v must be (batch, seqlen, heads, head_dim)")
+    _expect(k, (q.shape[0], k.shape[1], k.shape[2], q.shape[3]), "k")
+    _expect(v, k.shape, "v")
+    if k.shape[2] == 0 or q.shape[2] % k.shape[2]:
+        raise RuntimeError("the query heads must be a multiple of the key/value heads")
+
+
 def _register_python_parts() -> None:
     @torch.library.register_fake("fav::fwd")
     def _fwd_fake(q, k, v, causal, sm_scale):
+        _check_qkv(q, k, v)
         B, S, H, _ = q.shape
         return q.new_empty(q.shape), q.new_empty((B, H, S), dtype=torch.float32)
 
     @torch.library.register_fake("fav::bwd")
     def _bwd_fake(dout, q, k, v, out, lse, causal, sm_scale, deterministic=False):
+        _check_qkv(q, k, v)
+        _expect(dout, q.shape, "dout")
+        _expect(out, q.shape, "out")
+        _expect(lse, (q.shape[0], q.shape[2], q.shape[1]), "lse")
         return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
 
     @torch.library.register_fake("fav::merge_")
     def _merge_fake(acc_o, acc_lse, o, lse, first):
+        _expect(acc_o, o.shape, "acc_o")
+        _expect(lse, (o.shape[0], o.shape[2], o.shape[1]), "lse")
+        _expect(acc_lse, lse.shape, "acc_lse")
         return None
 
     def _setup(ctx, inputs, output):

@@ -125,9 +125,9 @@ def _exchange(sends, group, rank: int, world: int):
     the same shapes from rank-1 (one batched NCCL call); returns (recvs, works)."""
     nxt, prv = _peers(group, rank, world)
     recvs = [torch.empty_like(t) for t in sends]
-    ops = [dist.P2POp(dist.isend, t, nxt, group) for t in sends]
-    ops += [dist.P2POp(dist.irecv, t, prv, group) for t in recvs]
-    return recvs, dist.batch_isend_irecv(ops)
+    p2p = [dist.P2POp(dist.isend, t, nxt, group) for t in sends]
+    p2p += [dist.P2POp(dist.irecv, t, prv, group) for t in recvs]
+    return recvs, dist.batch_isend_irecv(p2p)
 
 
 def _finish(works):
@@ -239,9 +239,9 @@ def _ring_backward(do2, q2, k2, v2, o2, lse2, causal, scale, group):
                      for _ in range(2 * len(chunks))]
             g_dst = dist.get_global_rank(group, dst) if group is not None else dst
             g_peer = dist.get_global_rank(group, peer) if group is not None else peer
-            ops_ = [dist.P2POp(dist.isend, t, g_dst, group) for t in sends]
-            ops_ += [dist.P2POp(dist.irecv, t, g_peer, group) for t in recvs]
-            works = dist.batch_isend_irecv(ops_) if ops_ else []
+            p2p = [dist.P2POp(dist.isend, t, g_dst, group) for t in sends]
+            p2p += [dist.P2POp(dist.irecv, t, g_peer, group) for t in recvs]
+            works = dist.batch_isend_irecv(p2p) if p2p else []
             inflight = (works, recvs, chunks, sends)
         if pending is not None:
             recvs_kv, works_kv = pending

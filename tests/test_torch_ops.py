@@ -34,6 +34,39 @@ def test_fake_shapes_on_meta(Hkv, Sk):
     assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == k.shape
 
 
+def _bad_calls(dev):
+    """Direct operator calls whose tensors disagree with q / k: each must raise
+    (the C ABI takes every extent from q and k)."""
+    mk = lambda *s: torch.zeros(s, dtype=torch.float16, device=dev)  # noqa: E731
+    q, k, o = mk(1, 128, 4, 64), mk(1, 128, 2, 64), mk(1, 128, 4, 64)
+    lse = torch.zeros((1, 4, 128), dtype=torch.float32, device=dev)
+    return [
+        lambda: torch.ops.fav.fwd(q, mk(1, 128, 3, 64), mk(1, 128, 3, 64), True, 0.125),
+        lambda: torch.ops.fav.fwd(q, mk(1, 128, 2, 32), mk(1, 128, 2, 32), True, 0.125),
+        lambda: torch.ops.fav.fwd(q, k, mk(1, 64, 2, 64), True, 0.125),
+        lambda: torch.ops.fav.bwd(mk(1, 64, 4, 64), q, k, k, o, lse, True, 0.125),
+        lambda: torch.ops.fav.bwd(o, q, k, k, mk(1, 128, 4, 32), lse, True, 0.125),
+        lambda: torch.ops.fav.bwd(o, q, k, k, o, lse[:, :, :64], True, 0.125),
+        lambda: torch.ops.fav.merge_(o.float(), lse[:, :2], o, lse, False),
+    ]
+
+
+def test_shape_mismatch_raises_on_meta():
+    ops.load()
+    for call in _bad_calls("meta"):
+        with pytest.raises(RuntimeError):
+            call()
+
+
+@pytest.mark.gpu
+def test_shape_mismatch_raises_on_cuda():
+    ops.load()
+    for call in _bad_calls("cuda"):
+        with pytest.raises(RuntimeError):
+            call()
+    torch.cuda.synchronize()
+
+
 @pytest.mark.gpu
 def test_opcheck():
     ops.load()

@@ -77,6 +77,11 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
     cmd += ["-o", tmp, f"-L{HERE}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN"]
     cmd += [f"-L{d}" for d in libdirs]
     cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda"]
+    # The shared libstdc++ that torch itself uses, named explicitly: a toolchain
+    # whose libstdc++.so link is missing would otherwise fall back to
+    # libstdc++.a and put a second, uninitialised copy of the iostream / locale
+    # code into this library (torch's error messages then crash in it).
+    cmd += ["-l:libstdc++.so.6"]
     if verbose:
         print(" ".join(cmd))
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -84,8 +89,19 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
         sys.stderr.write(res.stdout + res.stderr)
     if res.returncode != 0:
         raise RuntimeError(f"g++ failed with exit code {res.returncode}")
+    if _has_static_libstdcxx(tmp):
+        os.remove(tmp)
+        raise RuntimeError(f"{cxx} linked libstdc++ statically into {out}; "
+                           "use a g++ whose libstdc++.so is installed (CXX=...)")
     os.replace(tmp, out)
     return out
+
+
+def _has_static_libstdcxx(path: str) -> bool:
+    """True if `path` carries libstdc++'s own locale instantiations, i.e. a
+    static copy of libstdc++ rather than a reference to libstdc++.so.6."""
+    with open(path, "rb") as f:
+        return b"locale_inst.cc" in f.read()
 
 
 def build(force: bool = False, verbose: bool = False) -> str:

@@ -22,6 +22,15 @@ def test_ops_library_registers_operators():
     assert "bool causal" in schema and "float sm_scale" in schema
 
 
+def test_ops_library_uses_shared_libstdcxx():
+    """A static copy of libstdc++ inside the operator library crashed when torch
+    formatted one of its error messages (two copies of the locale machinery in
+    one process)."""
+    from flash_attn_volta_b200 import build
+    ops.load()
+    assert not build._has_static_libstdcxx(build.ops_path())
+
+
 @pytest.mark.parametrize("Hkv,Sk", [(8, 300), (2, 77)])
 def test_fake_shapes_on_meta(Hkv, Sk):
     ops.load()

@@ -277,7 +277,10 @@ def ring_flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: b
     """Attention over a sequence sharded across the ranks of `group` (zigzag).
 
     Args:
-        q, k, v: this rank's zigzag shard, (B, 2*C, H, D) — see zigzag_shard.
+        q: this rank's zigzag shard, (B, 2*C, H, D) — see zigzag_shard.
+        k, v: the same rows of K and V, (B, 2*C, H_kv, D) with H % H_kv == 0
+            (grouped-query / multi-query attention: query head h reads K/V head
+            h // (H // H_kv); the K/V blocks travel with H_kv heads).
         causal: top-left causal mask over the full (unsharded) sequence.
         sm_scale: softmax scale (default 1/sqrt(D)).
         group: process group (default: the world).
@@ -286,5 +289,9 @@ def ring_flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: b
     """
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
-    assert q.shape == k.shape == v.shape and q.shape[1] % 2 == 0
+    assert k.shape == v.shape and q.dim() == 4 and q.shape[1] % 2 == 0
+    assert q.shape[:2] == k.shape[:2] and q.shape[3] == k.shape[3], \
+        "q and k/v must have the same batch, sequence shard and head_dim"
+    assert k.shape[2] > 0 and q.shape[2] % k.shape[2] == 0, \
+        "the query heads must be a multiple of the key/value heads"
     return _RingFlashAttnFn.apply(q, k, v, causal, sm_scale, group)

@@ -17,13 +17,24 @@ from oracle.attention_oracle import attention_bwd, attention_bwd_given_lse, atte
 from tests.helpers import make_inputs, maxdiff
 
 
+def _expand(q, k, v):
+    rep = q.shape[2] // k.shape[2]
+    return rep, k.repeat_interleave(rep, dim=2), v.repeat_interleave(rep, dim=2)
+
+
 def _oracle_block_fwd(q, k, v, causal, scale):
+    _, k, v = _expand(q, k, v)
     o, lse = attention_fwd(q, k, v, causal, scale, dtype=torch.float64)
     return o.float(), lse.float()
 
 
 def _oracle_block_bwd(do, q, k, v, o, lse, causal, scale):
-    return tuple(t.float() for t in attention_bwd_given_lse(do, q, k, v, o, lse, causal, scale))
+    """Grouped K/V: the gradients of the expanded heads summed over each group."""
+    B, C, Hkv, D = k.shape
+    rep, k, v = _expand(q, k, v)
+    dq, dk, dv = attention_bwd_given_lse(do, q, k, v, o, lse, causal, scale)
+    dk, dv = (t.reshape(B, C, Hkv, rep, D).sum(3) for t in (dk, dv))
+    return dq.float(), dk.float(), dv.float()
 
 
 def _free_port():
@@ -34,13 +45,19 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, causal, out_q):
+def _inputs(hkv):
+    """(B=2, S=64, H=4, D=16); K and V with `hkv` heads."""
+    q, k, v, do = [t.float() for t in make_inputs(2, 64, 4, 16, seed=5)]
+    return q, k[:, :, :hkv].contiguous(), v[:, :, :hkv].contiguous(), do
+
+
+def _worker(rank, world, port, causal, hkv, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ring.block_fwd, ring.block_bwd = _oracle_block_fwd, _oracle_block_bwd
-        q, k, v, do = [t.float() for t in make_inputs(2, 64, 2, 16, seed=5)]
+        q, k, v, do = _inputs(hkv)
         shard = lambda t: ring.zigzag_shard(t, rank, world).requires_grad_()
         qs, ks, vs = shard(q), shard(k), shard(v)
         o = ring.ring_flash_attn(qs, ks, vs, causal=causal)
@@ -50,13 +67,15 @@ def _worker(rank, world, port, causal, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
-@pytest.mark.parametrize("causal", [True, False])
-def test_ring_matches_full_attention(world, causal):
+@pytest.mark.parametrize("world,causal,hkv", [
+    (1, True, 4), (1, False, 4), (2, True, 4), (2, False, 4), (4, True, 4), (4, False, 4),
+    (2, True, 2), (4, True, 1), (2, False, 1)])
+def test_ring_matches_full_attention(world, causal, hkv):
+    """hkv < 4: grouped-query (2) and multi-query (1) K/V."""
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, causal, out_q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, causal, hkv, out_q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -65,9 +84,12 @@ def test_ring_matches_full_attention(world, causal):
         p.join(timeout=60)
         assert p.exitcode == 0
     o, dq, dk, dv = (ring.zigzag_unshard([torch.from_numpy(r[i]) for r in res]) for i in range(1, 5))
-    q, k, v, do = [t.float() for t in make_inputs(2, 64, 2, 16, seed=5)]
-    o_ref, _ = attention_fwd(q, k, v, causal, dtype=torch.float64)
-    g_ref = attention_bwd(do, q, k, v, causal)
+    q, k, v, do = _inputs(hkv)
+    rep, ke, ve = _expand(q, k, v)
+    o_ref, _ = attention_fwd(q, ke, ve, causal, dtype=torch.float64)
+    dq_r, dk_r, dv_r = attention_bwd(do, q, ke, ve, causal)
+    B, S, _, D = k.shape
+    g_ref = (dq_r, dk_r.reshape(B, S, hkv, rep, D).sum(3), dv_r.reshape(B, S, hkv, rep, D).sum(3))
     assert maxdiff(o, o_ref) < 1e-5
     for g, r in zip((dq, dk, dv), g_ref):
         assert maxdiff(g, r) < 1e-5

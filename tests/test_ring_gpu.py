@@ -36,6 +36,37 @@ def test_ring_one_rank_matches_kernel_and_oracle():
     assert maxdiff(o.detach(), full) <= TOL_O
 
 
+@pytest.mark.parametrize("hkv,dtype", [(2, torch.float16), (1, torch.bfloat16), (8, torch.bfloat16)])
+def test_ring_one_rank_gqa_and_bf16(hkv, dtype):
+    """Grouped-query (H_kv=2) and multi-query (H_kv=1) K/V and bf16 through the
+    ring, against the unsharded kernel on the same tensors (gradients of K/V
+    summed over each group by the kernels)."""
+    dev = torch.device("cuda", 0)
+    B, S, H, D = 2, 1536, 8, 64
+    g = torch.Generator(device=dev).manual_seed(30 + hkv)
+    q, do = (torch.randn((B, S, H, D), device=dev, generator=g).to(dtype) for _ in range(2))
+    k, v = (torch.randn((B, S, hkv, D), device=dev, generator=g).to(dtype) for _ in range(2))
+    # fp16: the parity tolerances; bf16 (8 mantissa bits, both sides rounded on
+    # different paths): 1e-2 on O, 2e-2 + |x|/64 on the gradients
+    bf16 = dtype == torch.bfloat16
+
+    def close(a, b, tol):
+        err = (a.double() - b.double()).abs()
+        return bool((err <= tol + (b.double().abs() / 64 if bf16 else 0)).all())
+
+    res = []
+    for fn in (ring.ring_flash_attn, flash_attn):
+        leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+        o = fn(*leaves, causal=True)
+        o.backward(do)
+        res.append((o.detach(),) + tuple(t.grad for t in leaves))
+    torch.cuda.synchronize(dev)
+    assert res[0][2].shape == (B, S, hkv, D)
+    assert close(res[0][0], res[1][0], 1e-2 if bf16 else TOL_O)
+    for a, b in zip(res[0][1:], res[1][1:]):
+        assert close(a, b, 2e-2 if bf16 else TOL_GRAD)
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_merge_kernel_matches_eager_merge(dtype):
     """fa_sm100_merge (torch.ops.fav.merge_) against the plain-torch merge, three

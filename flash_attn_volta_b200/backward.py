@@ -50,6 +50,8 @@ def flash_attn_backward(
     assert q.dtype in (torch.float16, torch.bfloat16)
     assert q.dtype == k.dtype == v.dtype == o.dtype == do.dtype
     assert lse.dtype == torch.float32
+    assert q.device == k.device == v.device == o.device == do.device == lse.device, \
+        "all tensors must be on the same device"
     assert q.shape == o.shape == do.shape
     Hkv = _kv_heads(q, k, v)
     B, N, H, D = q.shape

@@ -87,6 +87,51 @@ def load_peaks():
     return 1590.0, 1400.0, "fallback"
 
 
+def load_hbm_peak():
+    """Measured HBM copy bandwidth (GB/s) and its kind."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            v = json.load(f).get("hbm_gbs")
+        if v:
+            return float(v), "measured"
+    return 6650.0, "fallback"
+
+
+def merge_roofline(dev, rows, H, D, reps=20):
+    """fa_sm100_merge (the ring's LSE merge) on one block of the ring's size:
+    B=1, `rows` query rows, H heads, fp16 block output, not the first block.
+    Algorithmic bytes per launch: read the fp32 running O and the block's O,
+    write the running O (10 B per element), and per row read both LSEs and write
+    one (12 B).  Median of `reps` CUDA-event timed launches; the tensors are
+    larger than L2."""
+    from flash_attn_volta_b200 import ops
+    ops.load()
+    acc_o = torch.zeros((1, rows, H, D), device=dev, dtype=torch.float32)
+    acc_lse = torch.zeros((1, H, rows), device=dev, dtype=torch.float32)
+    o = torch.randn((1, rows, H, D), device=dev, dtype=torch.float16)
+    lse = torch.randn((1, H, rows), device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        torch.ops.fav.merge_(acc_o, acc_lse, o, lse, False)
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        torch.ops.fav.merge_(acc_o, acc_lse, o, lse, False)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = float(statistics.median(times))
+    nbytes = rows * H * D * (4 + 2 + 4) + rows * H * (4 + 4 + 4)
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    peak, kind = load_hbm_peak()
+    return {"kernel": "fa_merge_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "peak_kind": f"{kind} HBM copy",
+            "bytes_per_launch": nbytes, "median_ms": ms,
+            "shape": {"B": 1, "rows": rows, "H": H, "D": D}}
+
+
 def gen_shard(B0, B1, S, H, D, amp, device, seed_base=1234):
     """q, k, v, dO for batches [B0, B1) — each batch index has its own seed so
     every GPU count sees the same global tensors."""
@@ -898,7 +943,7 @@ def run_ring(args):
     fwd0, bwd0 = ring.block_fwd, ring.block_bwd
 
     def fwd_counted(*a):
-        counts[0] += 1
+        counts[0] += 2  # the block's forward kernel and its merge kernel
         return fwd0(*a)
 
     def bwd_counted(*a):
@@ -917,11 +962,13 @@ def run_ring(args):
     total = 2.5 * flops_fwd(B, S, H, D, causal) * args.steps
     value = total / (ms * 1e-3) / 1e12
     peak_burst, peak_sus, peak_kind = load_peaks()
+    merge = merge_roofline(dev, S // (2 * world), H, D) if rank == 0 else None
     if rank == 0:
         print(json.dumps({
             "metric": "attention fwd+bwd TFLOP/s", "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "merge_roofline": merge,
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "c5long", "B": B, "S": S, "H": H, "D": D, "causal": causal,
                        "parallelism": f"ring-cp{world} (zigzag)",

@@ -130,14 +130,19 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, out_q):
+def _two_gpu_inputs(hkv):
+    q, k, v, do = make_inputs(1, 4096, 4, 128, seed=12)
+    return q, k[:, :, :hkv].contiguous(), v[:, :, :hkv].contiguous(), do
+
+
+def _worker(rank, world, port, hkv, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
     try:
         dev = torch.device("cuda", rank)
-        q, k, v, do = make_inputs(1, 4096, 4, 128, seed=12)
+        q, k, v, do = _two_gpu_inputs(hkv)
         sh = lambda t: ring.zigzag_shard(t, rank, world).to(dev)
         qs, ks, vs = (sh(t).requires_grad_() for t in (q, k, v))
         o = ring.ring_flash_attn(qs, ks, vs, causal=True)
@@ -150,12 +155,14 @@ def _worker(rank, world, port, out_q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ring_two_gpus_matches_oracle():
+@pytest.mark.parametrize("hkv", [4, 2])
+def test_ring_two_gpus_matches_oracle(hkv):
+    """hkv=2: grouped-query K/V blocks travel between the ranks with 2 heads."""
     world = 2
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, out_q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, hkv, out_q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([out_q.get(timeout=300) for _ in range(world)], key=lambda x: x[0])
@@ -163,9 +170,19 @@ def test_ring_two_gpus_matches_oracle():
         p.join(timeout=120)
         assert p.exitcode == 0
     o, dq, dk, dv = (ring.zigzag_unshard([torch.from_numpy(r[i]) for r in res]) for i in range(1, 5))
-    q, k, v, do = make_inputs(1, 4096, 4, 128, seed=12)
+    q, k, v, do = _two_gpu_inputs(hkv)
+    rep = 4 // hkv
+    ke, ve = k.repeat_interleave(rep, dim=2), v.repeat_interleave(rep, dim=2)
     heads = [(0, 1), (0, 2)]
-    ref = oracle_heads(q, k, v, do, True, 1 / math.sqrt(128), heads)
+    ref = oracle_heads(q, ke, ve, do, True, 1 / math.sqrt(128), heads)
     assert maxdiff(pick_heads(o, heads), ref["o"]) <= TOL_O
-    for g, n in zip((dq, dk, dv), ("dq", "dk", "dv")):
-        assert maxdiff(pick_heads(g, heads), ref[n]) <= TOL_GRAD
+    assert maxdiff(pick_heads(dq, heads), ref["dq"]) <= TOL_GRAD
+    if hkv == 4:
+        for g, n in zip((dk, dv), ("dk", "dv")):
+            assert maxdiff(pick_heads(g, heads), ref[n]) <= TOL_GRAD
+    else:
+        # K/V head j gathers the gradients of query heads rep*j .. rep*j + rep - 1
+        full = oracle_heads(q, ke, ve, do, True, 1 / math.sqrt(128), [(0, 2), (0, 3)])
+        for g, n in ((dk, "dk"), (dv, "dv")):
+            ref_kv = full[n][0] + full[n][1]  # query heads 2 and 3 -> K/V head 1
+            assert maxdiff(g[0, :, 1], ref_kv) <= TOL_GRAD

@@ -202,6 +202,29 @@ def test_empty_sequence():
     assert dq.shape == q.shape
 
 
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_empty_batch_and_no_keys(deterministic):
+    """B = 0 gives empty outputs; N_k = 0 keys with N_q > 0 queries makes every
+    row fully masked: O = 0, LSE = +inf (the reference's convention) and zero
+    gradients, without a kernel launch reading empty tensors."""
+    from flash_attn_volta_b200 import flash_attn, flash_attn_backward, flash_attn_forward
+    q0 = torch.zeros(0, 64, 2, 64, dtype=torch.float16, device=DEV)
+    o0, lse0 = flash_attn_forward(q0, q0, q0, causal=True, return_softmax_lse=True)
+    assert o0.shape == q0.shape and lse0.shape == (0, 2, 64)
+    g = flash_attn_backward(q0, q0, q0, q0, o0, lse0, causal=True, deterministic=deterministic)
+    assert all(t.shape == q0.shape for t in g)
+    q = torch.randn(2, 40, 4, 32, dtype=torch.float16, device=DEV).requires_grad_()
+    kv = torch.zeros(2, 0, 2, 32, dtype=torch.float16, device=DEV)
+    k, v = kv.clone().requires_grad_(), kv.clone().requires_grad_()
+    o, lse = flash_attn_forward(q.detach(), kv, kv, return_softmax_lse=True)
+    assert (o == 0).all() and torch.isposinf(lse).all()
+    out = flash_attn(q, k, v, deterministic=deterministic)
+    out.backward(torch.ones_like(out))
+    torch.cuda.synchronize(DEV)
+    assert (out == 0).all() and (q.grad == 0).all()
+    assert k.grad.shape == kv.shape and v.grad.shape == kv.shape
+
+
 @pytest.mark.parametrize("causal", [False, True])
 def test_repeated_runs_bit_identical(causal):
     """Intermittent ordering bugs show up as run-to-run differences: the forward

@@ -225,6 +225,27 @@ def test_empty_batch_and_no_keys(deterministic):
     assert k.grad.shape == kv.shape and v.grad.shape == kv.shape
 
 
+def test_largest_batch_times_heads():
+    """B * H = 65535, the most the library accepts (a grid dimension of the
+    backward's prep / conversion kernels): fwd + bwd against the oracle on
+    sampled (b, h); one more raises instead of launching."""
+    from flash_attn_volta_b200 import flash_attn
+    B, S, H, D = 13107, 24, 5, 16  # 13107 * 5 = 65535
+    q, k, v, do = make_inputs(B, S, H, D, seed=8)
+    leaves = [t.to(DEV).requires_grad_() for t in (q, k, v)]
+    out = flash_attn(*leaves, causal=True)
+    out.backward(do.to(DEV))
+    torch.cuda.synchronize(DEV)
+    heads = [(0, 0), (6553, 2), (B - 1, H - 1)]
+    ref = oracle_heads(q, k, v, do, True, 1 / math.sqrt(D), heads)
+    assert maxdiff(pick_heads(out.detach().cpu(), heads), ref["o"]) <= TOL_O
+    for g, n in zip(leaves, ("dq", "dk", "dv")):
+        assert maxdiff(pick_heads(g.grad.cpu(), heads), ref[n]) <= TOL_GRAD
+    big = torch.zeros(65536, 8, 1, 16, dtype=torch.float16, device=DEV)
+    with pytest.raises(RuntimeError):
+        flash_attn(big, big, big)
+
+
 @pytest.mark.parametrize("causal", [False, True])
 def test_repeated_runs_bit_identical(causal):
     """Intermittent ordering bugs show up as run-to-run differences: the forward

@@ -16,15 +16,19 @@ Extra keys beside the base contract:
                steps overlap the compute: three streams, double-buffered inputs).
   roofline     the dominant kernel (the main backward kernel) timed alone with
                CUDA events; achieved = its algorithmic tensor FLOPs (5 GEMMs,
-               2.5 x F_fwd) / its mean duration; peak = MEASURED_PEAKS.json.
-  cpu_baseline the CPU oracle (restatement of the reference's fp32 eager path)
-               on one (batch, head) pair of the same workload, rank 0, N=1.
+               2.5 x F_fwd) / its median duration; peak = MEASURED_PEAKS.json.
+  cpu_baseline the reference's fp32 eager path (flash_attn_volta/ref.py from the
+               unmodified package in baseline/_ref; the oracle restatement of it
+               only where that copy is missing) on 8 (batch, head) pairs of the
+               same workload, rank 0, N=1, extrapolated by FLOPs.
   headline_c3b the headline config (B=1, S=4096, H=8, D=128, causal) at N=1,
                with config 3's D=64 case (B=1, S=4096, H=16) under "c3a": fwd+bwd
                through the autograd API and the forward with LSE alone.
   clocks       nvidia-smi samples taken during the timed region.
---impl reference times the reference's CPU path (the oracle port) on the host
-cores, each step = fwd+bwd of one (batch, head) pair of the workload.
+--impl reference times the same CPU path on all host cores, each step = fwd+bwd
+of 8 (batch, head) pairs of the workload; under torchrun only rank 0 runs it.
+--impl reference-triton (informational) runs the reference's Triton kernels on
+the GPU through its public API.
 """
 from __future__ import annotations
 

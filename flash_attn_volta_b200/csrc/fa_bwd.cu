@@ -21,7 +21,7 @@
 //   fa_bwd_pre   delta = rowsum(O * dO), the extra K-step rows of Q and dO in the
 //                MMA's no-swizzle K-major layout, zero the dQ accumulator.
 //   fa_bwd_main  a CTA walks a list of 128-row key/value tiles of the (batch,
-//                K/V head) pairs (persistent, one CTA per SM, for at most 4
+//                K/V head) pairs (persistent, one CTA per SM, for at most 16
 //                tiles per SM; else one CTA per tile); each tile loops over
 //                query tiles of BM rows (64 for D=128, else 128).  On the
 //                persistent grid the next tile's K/V load, Q/dO loads and first

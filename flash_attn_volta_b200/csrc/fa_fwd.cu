@@ -9,7 +9,7 @@
 //
 // A CTA walks a list of 128-row query tiles of the (batch, head) pairs (round
 // r takes tile r * grid + CTA, in reverse CTA order on odd rounds, over a
-// longest-first order).  Small problems (at most 4 tiles per SM) run one
+// longest-first order).  Problems of at most 16 tiles per SM run one
 // persistent CTA per SM, so the set-up is paid once per SM and the next tile's
 // Q load and first S = Q K^T overlap this tile's last softmax step and its
 // epilogue; larger ones run one CTA per tile.  Tensor memory (512

@@ -98,11 +98,17 @@ inline int sm_count() {
   return n;
 }
 // Grid of a tile-list kernel: one CTA per SM walking the list when there are
-// at most kPersistMaxTilesPerSm tiles per SM (small problems, where the set-up
-// and drain of each CTA and the balance of the last wave matter most),
-// otherwise one CTA per tile in list order.  Measured at B=8, S=8192, H=32,
-// D=128: the persistent grid lost 10 % per fwd+bwd step.
-constexpr int kPersistMaxTilesPerSm = 4;
+// at most kPersistMaxTilesPerSm tiles per SM (where the set-up and drain of
+// each CTA and the balance of the last wave matter most; the persistent grid
+// overlaps a tile's epilogue with the next tile's first loads and MMAs),
+// otherwise one CTA per tile in list order.  Measured on one B200 (D=128,
+// causal, medians of 15 launches): the forward at B=8, S=2048, H=16 (13.8
+// tiles per SM) 0.229 -> 0.194 ms and at B=1, S=8192, H=16 (6.9 per SM) 0.323
+// -> 0.303 ms with the persistent grid, the backward main kernel there 0.528
+// -> 0.515 ms and 0.80 -> 0.79 ms; at 27.7 tiles per SM (B=2, S=8192, H=32)
+// the persistent forward lost 5 %, and at B=8, S=8192, H=32 (110 per SM) the
+// persistent backward lost 12 % (static tile split: the last CTAs finish late).
+constexpr int kPersistMaxTilesPerSm = 16;
 inline int tile_grid(int ntiles, int nsm) {
   return ntiles <= kPersistMaxTilesPerSm * nsm ? (ntiles < nsm ? ntiles : nsm) : ntiles;
 }

@@ -1,6 +1,6 @@
 """The two launch shapes of the main kernels give the same results.
 
-Both main kernels walk a list of tiles: with at most 4 tiles per SM the grid is
+Both main kernels walk a list of tiles: with at most 16 tiles per SM the grid is
 one persistent CTA per SM (several rounds of tiles per CTA), otherwise one CTA
 per tile.  A tile's arithmetic does not depend on which CTA runs it, so O, LSE,
 dK and dV of a head must be bit-identical whether the head is computed among
@@ -37,13 +37,14 @@ def _fwd_bwd(q, k, v, do, causal):
 
 
 def test_one_cta_per_tile_matches_persistent_grid():
-    B, S, H, D = 1, 4096, 40, 128  # 40 x 32 = 1280 tiles: one CTA per tile
+    # 80 x 32 = 2560 tiles (more than 16 per SM on 148 SMs): one CTA per tile
+    B, S, H, D = 1, 4096, 80, 128
     g = torch.Generator().manual_seed(77)
     q, k, v, do = [(torch.randn((B, S, H, D), generator=g) * 0.5).half().to(DEV)
                    for _ in range(4)]
     full = _fwd_bwd(q, k, v, do, True)
     # an 8-head slice (256 tiles: two persistent rounds) and one head (32 tiles)
-    for lo, hi in ((8, 16), (39, 40)):
+    for lo, hi in ((8, 16), (79, 80)):
         part = _fwd_bwd(*(t[:, :, lo:hi].contiguous() for t in (q, k, v, do)), True)
         o_f, lse_f, dq_f, dk_f, dv_f = full
         o_p, lse_p, dq_p, dk_p, dv_p = part

@@ -33,6 +33,7 @@ the GPU through its public API.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import csv
 import io
 import json
@@ -242,6 +243,42 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
                 "samples": len(rows), "source": "nvidia-smi, 50 ms"}
+
+
+def gpu_local_cpus(index):
+    """CPUs that NVML reports as closest to CUDA device `index` (those this
+    process may run on), or an empty set when that is unknown."""
+    try:
+        import pynvml
+        p = torch.cuda.get_device_properties(index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 1) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        return cpus & os.sched_getaffinity(0)
+    except Exception:
+        return set()
+
+
+@contextlib.contextmanager
+def near_gpu(index):
+    """Run the body on the CPUs local to GPU `index`, so that host memory first
+    touched there (pinned buffers: their pages are mapped when allocated) sits
+    on the GPU's NUMA node; the previous affinity is restored on exit.  Yields
+    whether the GPU's CPUs were known."""
+    cpus = gpu_local_cpus(index)
+    old = os.sched_getaffinity(0)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    try:
+        yield bool(cpus)
+    finally:
+        if cpus:
+            os.sched_setaffinity(0, old)
 
 
 # ----------------------------------------------------------------------- CPU path
@@ -486,8 +523,13 @@ def run_ours(args, wl):
     # its results (O, dQ, dK, dV) back out, inside the timed region.  Three
     # streams and double-buffered device inputs let step i+1's copy-in and step
     # i-1's copy-out run while step i computes, as a training pipeline would.
-    hin = [t.detach().cpu().pin_memory() for t in (q, k, v, do)]
-    hout = [[torch.empty_like(hin[0]).pin_memory() for _ in range(4)] for _ in range(2)]
+    # The pinned buffers are allocated from the GPU's own CPUs so that their
+    # pages sit on its NUMA node: with 8 ranks on a two-socket host, buffers
+    # placed wherever a rank's thread happened to run would send half of the
+    # copies across the socket link.
+    with near_gpu(dev.index) as host_local:
+        hin = [t.detach().cpu().pin_memory() for t in (q, k, v, do)]
+        hout = [[torch.empty_like(hin[0]).pin_memory() for _ in range(4)] for _ in range(2)]
     dbuf = [[torch.empty_like(q) for _ in range(4)] for _ in range(2)]
     for bset in dbuf:
         for t_ in bset[:3]:
@@ -641,7 +683,10 @@ def run_ours(args, wl):
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nb,
                     "d2h_bytes_per_step": 4 * nb, "steps": e2e_steps,
                     "overlap": "copy-in of step i+1 and copy-out of step i-1 run beside "
-                               "step i's compute (three streams, double-buffered inputs)"},
+                               "step i's compute (three streams, double-buffered inputs)",
+                    "host_buffers": ("pinned, on the GPU's NUMA node (allocated from the CPUs "
+                                     "NVML reports local to it)") if host_local
+                                    else "pinned, default placement (GPU-local CPUs unknown)"},
             "roofline": {"bound": "tensor", "kernel": f"fa_bwd_main_kernel<{D}>",
                          "achieved": k_tflops, "peak": peak_burst, "unit": "TFLOP/s",
                          "frac": k_tflops / peak_burst,

@@ -41,3 +41,13 @@ def test_max_over_ranks_timing():
     res = [q.get(timeout=60) for _ in range(2)]
     [p.join(timeout=30) for p in ps]
     assert all(v == 11.0 for _, v in res)
+
+
+def test_near_gpu_restores_affinity_and_tolerates_unknown_gpu():
+    # Without a GPU (or NVML) the GPU-local CPU set is unknown: the context
+    # runs the body unchanged and leaves the process affinity as it was.
+    before = os.sched_getaffinity(0)
+    with bench.near_gpu(0) as known:
+        if not known:
+            assert os.sched_getaffinity(0) == before
+    assert os.sched_getaffinity(0) == before

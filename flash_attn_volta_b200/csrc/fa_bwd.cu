@@ -22,7 +22,8 @@
 //                MMA's no-swizzle K-major layout, zero the dQ accumulator.
 //   fa_bwd_main  a CTA walks a list of 128-row key/value tiles of the (batch,
 //                K/V head) pairs (persistent, one CTA per SM, for at most 16
-//                tiles per SM; else one CTA per tile); each tile loops over
+//                tiles per SM, 8 for causal sequences longer than 4096; else
+//                one CTA per tile); each tile loops over
 //                query tiles of BM rows (64 for D=128, else 128).  On the
 //                persistent grid the next tile's K/V load, Q/dO loads and first
 //                S^T / dP^T MMAs overlap this tile's last iterations and its
@@ -870,7 +871,8 @@ static int launch_bwd_main(const BwdArgs& a, cudaStream_t stream) {
   const int ntiles = a.B * a.Hkv * ((a.Sk + C::BN - 1) / C::BN);
   const int nsm = sm_count();
   if (nsm <= 0) return FA_ERR_DEVICE;
-  const int g = tile_grid(ntiles, nsm);
+  const int g =
+      tile_grid(ntiles, nsm, persist_max_tiles(a.causal != 0, a.Sq > a.Sk ? a.Sq : a.Sk));
   dim3 grid(g);
   const cudaError_t e = launch_pdl(
       fa_bwd_main_kernel<D, T, DQ>, grid, dim3(C::THREADS), C::SMEM, stream, *a.tm_q, *a.tm_do,

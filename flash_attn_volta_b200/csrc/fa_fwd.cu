@@ -9,10 +9,10 @@
 //
 // A CTA walks a list of 128-row query tiles of the (batch, head) pairs (round
 // r takes tile r * grid + CTA, in reverse CTA order on odd rounds, over a
-// longest-first order).  Problems of at most 16 tiles per SM run one
-// persistent CTA per SM, so the set-up is paid once per SM and the next tile's
-// Q load and first S = Q K^T overlap this tile's last softmax step and its
-// epilogue; larger ones run one CTA per tile.  Tensor memory (512
+// longest-first order).  Problems of at most 16 tiles per SM (8 for causal
+// sequences longer than 4096) run one persistent CTA per SM, so the set-up is
+// paid once per SM and the next tile's Q load and first S = Q K^T overlap this
+// tile's last softmax step and its epilogue; larger ones run one CTA per tile.  Tensor memory (512
 // columns): S0 [0,128), S1 [128,256) — S = Q K_j^T double-buffered; P0
 // [256,320), P1 [320,384) — P (fp16 pairs) double-buffered; O [384, 384+D).
 // Because P has its own columns, nothing in the tensor-core stream waits for
@@ -593,7 +593,8 @@ static int launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
   const int ntiles = a.B * a.H * ((a.Sq + C::BM - 1) / C::BM);
   const int nsm = sm_count();
   if (nsm <= 0) return FA_ERR_DEVICE;
-  const int g = tile_grid(ntiles, nsm);
+  const int g =
+      tile_grid(ntiles, nsm, persist_max_tiles(a.causal != 0, a.Sq > a.Sk ? a.Sq : a.Sk));
   dim3 grid(g);
   const cudaError_t e = launch_pdl(fa_fwd_kernel<D, T>, grid, dim3(C::THREADS), C::SMEM, stream,
                                    *a.tm_q, *a.tm_k, *a.tm_v, static_cast<T*>(a.o), a.lse,

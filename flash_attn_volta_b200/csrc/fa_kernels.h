@@ -98,19 +98,27 @@ inline int sm_count() {
   return n;
 }
 // Grid of a tile-list kernel: one CTA per SM walking the list when there are
-// at most kPersistMaxTilesPerSm tiles per SM (where the set-up and drain of
-// each CTA and the balance of the last wave matter most; the persistent grid
+// at most persist_max_tiles() tiles per SM (where the set-up and drain of each
+// CTA and the balance of the last wave matter most; the persistent grid
 // overlaps a tile's epilogue with the next tile's first loads and MMAs),
-// otherwise one CTA per tile in list order.  Measured on one B200 (D=128,
-// causal, medians of 15 launches): the forward at B=8, S=2048, H=16 (13.8
-// tiles per SM) 0.229 -> 0.194 ms and at B=1, S=8192, H=16 (6.9 per SM) 0.323
-// -> 0.303 ms with the persistent grid, the backward main kernel there 0.528
-// -> 0.515 ms and 0.80 -> 0.79 ms; at 27.7 tiles per SM (B=2, S=8192, H=32)
-// the persistent forward lost 5 %, and at B=8, S=8192, H=32 (110 per SM) the
-// persistent backward lost 12 % (static tile split: the last CTAs finish late).
-constexpr int kPersistMaxTilesPerSm = 16;
-inline int tile_grid(int ntiles, int nsm) {
-  return ntiles <= kPersistMaxTilesPerSm * nsm ? (ntiles < nsm ? ntiles : nsm) : ntiles;
+// otherwise one CTA per tile in list order.  The static split of the
+// persistent grid balances tiles of one length well, and causal tiles of very
+// different lengths less so, hence a lower limit for long causal sequences.
+// Measured on one B200 (D=128, medians of 15 launches, persistent vs one CTA
+// per tile):
+//   B=8, S=2048, H=16 causal (13.8 tiles per SM): forward 0.229 -> 0.194 ms,
+//     backward main kernel 0.528 -> 0.515 ms; non-causal +10 % / +4 %
+//   B=1, S=8192, H=16 causal (6.9 per SM): forward 0.323 -> 0.303 ms,
+//     backward unchanged
+//   B=1, S=8192, H=32 (13.8 per SM): causal forward -4 %, backward -10 %;
+//     non-causal +7 % / +3 %
+//   B=2, S=8192, H=32 causal (27.7 per SM): forward -5 %
+//   B=8, S=8192, H=32 causal (110 per SM): backward -12 %.
+inline int persist_max_tiles(bool causal, int seqlen) {
+  return (causal && seqlen > 4096) ? 8 : 16;
+}
+inline int tile_grid(int ntiles, int nsm, int max_per_sm) {
+  return ntiles <= max_per_sm * nsm ? (ntiles < nsm ? ntiles : nsm) : ntiles;
 }
 // Heads per window of a tile list: 16 on the persistent grid (tiles dealt out
 // in one round have similar lengths), 8 with one CTA per tile (fewer heads'
